@@ -1,0 +1,362 @@
+"""Benchmark: sqrt-block attention forward+backward at B=1, H=16, T=16384, D=128, bf16.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward (sqb_fwd) and one backward (sqb_bwd) of the attention
+operator over the whole workload.  ``value`` is whole-job algorithmic HBM
+throughput in GB/s (compulsory bytes 12*B*H*T*D*2 + 8*B*H*T per step, summed
+over ranks, divided by the max-over-ranks device time).  Inputs (Q, K, V, dO:
+4 x 67 MB, plus O and the gradients) exceed the 126 MB L2, so no flush is
+needed between steps.  Multi-GPU: one process per GPU under torchrun, every
+rank runs its own 16 heads (weak scaling; the (batch, head) units are
+independent, so there is no data-path collective).
+
+``--impl reference`` times the CPU restatement of the operator (the
+reference repository has no implementation of it) on the host cores, on a
+bounded sample of the same workload (a subset of heads), and prints the same
+metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+METRIC = "sqrt-block attn fwd+bwd ms & HBM GB/s at T=16K; GPT-2 small train tokens/sec"
+B, H, T, D = 1, 16, 16384, 128
+ELT = 2  # bf16
+
+
+def algorithmic_bytes(B_, H_, T_, D_, elt=ELT, fwd=True, bwd=True):
+    n = B_ * H_ * T_
+    return (4 * n * D_ * elt + 4 * n if fwd else 0) + (8 * n * D_ * elt + 4 * n if bwd else 0)
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64,
+                     device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def make_inputs(seed, rank, device, dtype=torch.bfloat16, H_=H):
+    g = torch.Generator().manual_seed(seed * 1000 + rank)
+    return [torch.randn(B, T, H_, D, generator=g).to(dtype) for _ in range(4)]
+
+
+def cpu_sample_time(heads=1, reps=1):
+    """Time the oracle port (fp32 torch, all host threads) on `heads` heads of
+    the workload, forward+backward; returns (seconds per sample, threads)."""
+    from oracle.torch_port import sqrt_block_attention_ref
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    q, k, v, do = [torch.randn(1, heads, T, D, generator=g) for _ in range(4)]
+    best = None
+    for _ in range(reps):
+        qs, ks, vs = [x.clone().requires_grad_(True) for x in (q, k, v)]
+        t0 = time.perf_counter()
+        o, _ = sqrt_block_attention_ref(qs, ks, vs)
+        (o * do).sum().backward()
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return best, threads
+
+
+def run_reference(args, world, rank):
+    """CPU restatement of the operator, timed on the host cores."""
+    if rank != 0:
+        return
+    heads = 1
+    sample_bytes = algorithmic_bytes(B, heads, T, D)
+    cpu_sample_time(heads, 1)  # warm-up allocations and thread pool
+    times = []
+    for _ in range(max(args.warmup, 0)):
+        cpu_sample_time(heads, 1)
+    for _ in range(args.steps):
+        dt, threads = cpu_sample_time(heads, 1)
+        times.append(dt)
+    per = statistics.median(times)
+    gbs = sample_bytes / per / 1e9
+    full_ms = per * (H / heads) * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(full_ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "sqrt-block attention fwd+bwd", "B": B, "H": H, "T": T, "D": D,
+                   "block": 128, "parallelism": f"heads x {world} ranks (rank 0 timed)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{heads} of {H} heads per step, fp32 torch, "
+                                   "ms_per_step scaled to all heads"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    from llm_training_b200 import _lib
+    from llm_training_b200.ops import (read_status, sqrt_block_attention, sqrt_block_backward,
+                                       sqrt_block_forward)
+
+    dev = torch.device("cuda", local)
+    host = make_inputs(args.seed, rank, dev)
+    q, k, v, do = [x.to(dev) for x in host]
+    block = 128
+    impl = args.kernels
+    if impl == "auto":
+        try:
+            sqrt_block_forward(q[:, :256], k[:, :256], v[:, :256], block, None, "tcgen05")
+            impl = "tcgen05"
+        except _lib.SqrtBlockError:
+            impl = "simt"
+    launches_per_step = {"tcgen05": 2, "simt": 7}[impl]
+
+    stream = torch.cuda.current_stream(dev)
+    f_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    b_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+
+    def step(i=None):
+        if i is not None:
+            f_ev[2 * i].record(stream)
+        o, lse, kbar, vbar = sqrt_block_forward(q, k, v, block, None, impl)
+        if i is not None:
+            f_ev[2 * i + 1].record(stream)
+            b_ev[2 * i].record(stream)
+        dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, do, block, None, impl)
+        if i is not None:
+            b_ev[2 * i + 1].record(stream)
+        return o, dq
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = max_over_ranks(start.elapsed_time(end), world)
+    status = read_status(dev)
+    fwd_ms = statistics.mean(f_ev[2 * i].elapsed_time(f_ev[2 * i + 1]) for i in range(args.steps))
+    bwd_ms = statistics.mean(b_ev[2 * i].elapsed_time(b_ev[2 * i + 1]) for i in range(args.steps))
+
+    ms_per_step = total_ms / args.steps
+    step_bytes = algorithmic_bytes(B, H, T, D)
+    value = step_bytes * world / (ms_per_step * 1e-3) / 1e9
+
+    # end to end through the public autograd op, host (pinned) buffers in and out
+    pinned = [x.pin_memory() for x in host]
+    outs = [torch.empty(B, T, H, D, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+
+    def e2e_step():
+        qd, kd, vd, dod = [x.to(dev, non_blocking=True) for x in pinned]
+        for t in (qd, kd, vd):
+            t.requires_grad_(True)
+        o = sqrt_block_attention(qd, kd, vd, block, None, impl)
+        o.backward(dod)
+        for dst, src in zip(outs, (o.detach(), qd.grad, kd.grad, vd.grad)):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(1, min(args.steps, 5))
+    e_start.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world) / e_steps
+    h2d = sum(x.numel() * x.element_size() for x in pinned)
+    d2h = sum(x.numel() * x.element_size() for x in outs)
+
+    peak, peak_kind = load_peaks()
+    bwd_bytes = algorithmic_bytes(B, H, T, D, fwd=False)
+    fwd_bytes = algorithmic_bytes(B, H, T, D, bwd=False)
+    dom = ("backward", bwd_bytes, bwd_ms) if bwd_ms >= fwd_ms else ("forward", fwd_bytes, fwd_ms)
+    achieved = dom[1] / (dom[2] * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None, "kernel": dom[0],
+                "peak_source": peak_kind,
+                "fwd": {"ms": round(fwd_ms, 4),
+                        "GBps": round(fwd_bytes / (fwd_ms * 1e-3) / 1e9, 1)},
+                "bwd": {"ms": round(bwd_ms, 4),
+                        "GBps": round(bwd_bytes / (bwd_ms * 1e-3) / 1e9, 1)}}
+    traffic_path = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(traffic_path):
+        try:
+            roofline["traffic"] = json.load(open(traffic_path)).get(impl, {}).get(dom[0])
+        except Exception:
+            pass
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        heads = 1
+        dt, threads = cpu_sample_time(heads, 1)
+        cpu = {"value": round(algorithmic_bytes(B, heads, T, D) / dt / 1e9, 3), "unit": "GB/s",
+               "cores": threads, "kind": "port",
+               "sample": f"{heads} of {H} heads, fp32 torch fwd+bwd, {dt * 1e3:.0f} ms"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded per rank",
+            "config": {"workload": "sqrt-block attention fwd+bwd (sweep point T=16384)",
+                       "B": B, "H_per_rank": H, "T": T, "D": D, "block": block,
+                       "parallelism": f"heads x {world} ranks", "kernels": impl,
+                       "l2": "inputs 4 x 67 MB > 126 MB L2; no flush"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(step_bytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--kernels", choices=["auto", "tcgen05", "simt"], default="auto")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    args = ap.parse_args()
+    world, rank, local = init_dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,26 @@
+// sm_100a (B200) tensor-core kernels for sqrt-block attention: tcgen05.mma with
+// TMEM accumulators, operands staged in shared memory by TMA (no multicast).
+#pragma once
+
+#include <initializer_list>
+
+#include "sqb_internal.cuh"
+
+namespace sqb {
+
+// True when the tcgen05 kernels handle this problem and these tensor views
+// (bf16, supported D and block length, 16-byte aligned pointers and strides,
+// sm_100-class device).
+bool sm100_supported(const Problem& p, std::initializer_list<TensorView> views, const float* lse,
+                     const void* kbar, const void* vbar);
+
+int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,
+                  float* lse, void* kbar, void* vbar, uint8_t* ws, const WorkspaceLayout& wl,
+                  cudaStream_t stream);
+
+int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,
+                   TensorView dout, const float* lse, const void* kbar, const void* vbar,
+                   TensorView dq, TensorView dk, TensorView dv, uint8_t* ws,
+                   const WorkspaceLayout& wl, cudaStream_t stream);
+
+}  // namespace sqb

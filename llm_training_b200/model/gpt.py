@@ -1,0 +1,96 @@
+"""Minimal GPT-2 caller of the attention plugin (training configurations only).
+
+Mirrors the reference's model stack so that state-dict keys and numerics of the
+non-attention parts match: ``GPT`` (model/GPT.py:11-70: wte/wpe/drop/attn_blocks/
+ln_ in ``transformer``, tied ``lm_head``, N(0, 0.02) init, c_proj scaled by
+1/sqrt(2 n_layer)), ``Attention_Block`` (model/attention_block.py:6-25, pre-norm
+``x + attn(lm1(x)); x + mlp(lm2(x))``), ``MLP`` (model/mlp.py:5-16, tanh GELU)
+and ``LayerNorm`` (model/layer_norm.py:4-13, optional bias).  The attention is
+built through ``build_attention(config)`` exactly as the reference block does.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from .attention_registry import build_attention
+
+
+class LayerNorm(nn.Module):
+    def __init__(self, ndim, bias=True, eps=1e-5):
+        super().__init__()
+        self.ln = nn.LayerNorm(ndim, eps=eps)
+        if not bias:
+            self.ln.register_parameter("bias", None)
+
+    def forward(self, x):
+        return self.ln(x)
+
+
+class MLP(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        self.c_fc = nn.Linear(config.n_embd, 4 * config.n_embd, bias=config.bias)
+        self.gelu = nn.GELU(approximate="tanh")
+        self.c_proj = nn.Linear(4 * config.n_embd, config.n_embd, bias=config.bias)
+        self.drop = nn.Dropout(config.dropout)
+
+    def forward(self, x):
+        return self.drop(self.c_proj(self.gelu(self.c_fc(x))))
+
+
+class Attention_Block(nn.Module):  # noqa: N801  (reference class name)
+    def __init__(self, config):
+        super().__init__()
+        self.lm1 = LayerNorm(config.n_embd, bias=config.bias)
+        self.attn = build_attention(config)
+        self.lm2 = LayerNorm(config.n_embd, bias=config.bias)
+        self.mlp = MLP(config)
+
+    def forward(self, x):
+        x = x + self.attn(self.lm1(x))
+        x = x + self.mlp(self.lm2(x))
+        return x
+
+
+class GPT(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        assert config.vocab_size is not None
+        assert config.block_size is not None
+        self.config = config
+        self.transformer = nn.ModuleDict(dict(
+            wte=nn.Embedding(config.vocab_size, config.n_embd),
+            wpe=nn.Embedding(config.block_size, config.n_embd),
+            drop=nn.Dropout(config.dropout),
+            attn_blocks=nn.ModuleList([Attention_Block(config) for _ in range(config.n_layer)]),
+            ln_=LayerNorm(config.n_embd, bias=config.bias),
+        ))
+        self.lm_head = nn.Linear(config.n_embd, config.vocab_size, bias=False)
+        self.transformer.wte.weight = self.lm_head.weight
+        self.apply(self._init_weights)
+        for pn, p in self.named_parameters():
+            if pn.endswith("c_proj.weight"):
+                torch.nn.init.normal_(p, mean=0.0, std=0.02 / math.sqrt(2 * config.n_layer))
+
+    @staticmethod
+    def _init_weights(module):
+        if isinstance(module, nn.Linear):
+            torch.nn.init.normal_(module.weight, mean=0.0, std=0.02)
+            if module.bias is not None:
+                torch.nn.init.zeros_(module.bias)
+        elif isinstance(module, nn.Embedding):
+            torch.nn.init.normal_(module.weight, mean=0.0, std=0.02)
+
+    def forward(self, idx):
+        b, t = idx.size()
+        assert t <= self.config.block_size, (
+            f"Cannot forward sequence of length {t}, block size is only {self.config.block_size}")
+        pos = torch.arange(0, t, dtype=torch.long, device=idx.device)
+        x = self.transformer.drop(self.transformer.wte(idx) + self.transformer.wpe(pos))
+        for block in self.transformer.attn_blocks:
+            x = block(x)
+        return self.lm_head(self.transformer.ln_(x))

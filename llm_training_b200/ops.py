@@ -1,0 +1,168 @@
+"""PyTorch entry points of the sqrt-block attention CUDA library.
+
+``sqrt_block_attention(q, k, v)`` takes (B, T, H, D) CUDA views - exactly the
+``Linear(X).view(B, T, H, D)`` layout the plugin module produces - and returns
+O in the same (B, T, H, D) layout, differentiable through the library's
+backward.  PyTorch only supplies device memory, the current stream and
+autograd bookkeeping; all attention math runs in libsqrtblock.so.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import _lib
+
+__all__ = ["sqrt_block_attention", "sqrt_block_forward", "sqrt_block_backward", "read_status",
+           "block_geometry"]
+
+_DTYPES = {torch.float32: _lib.SQB_F32, torch.bfloat16: _lib.SQB_BF16}
+
+_ws_lock = threading.Lock()
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def block_geometry(T: int, block: int | None = None):
+    """(b, G, Gc): block length, blocks, complete blocks for T tokens."""
+    return _lib.geometry(T, block)
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device zero-initialised scratch, grown on demand.
+
+    The kernels keep it clean between calls (flags are epoch-stamped and the
+    summary-gradient accumulators are re-zeroed by their consumer), so it is
+    zeroed only when allocated.  Calls on one device must share one stream.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _workspaces.get(idx)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            _workspaces[idx] = ws
+        return ws
+
+
+def _strides(t: torch.Tensor):
+    return (t.stride(0), t.stride(1), t.stride(2))
+
+
+def _prep(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise RuntimeError(f"sqrt_block_attention: {name} must be a CUDA tensor "
+                           "(the op has no CPU implementation)")
+    if t.dim() != 4:
+        raise ValueError(f"sqrt_block_attention: {name} must be (B, T, H, D), got {tuple(t.shape)}")
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    return t
+
+
+def _impl_code(impl: str) -> int:
+    try:
+        return _lib.IMPLS[impl]
+    except KeyError:
+        raise ValueError(f"impl must be one of {sorted(_lib.IMPLS)}, got {impl!r}") from None
+
+
+def sqrt_block_forward(q, k, v, block=None, scale=None, impl="auto"):
+    """Forward only -> (o, lse, kbar, vbar).
+
+    q, k, v: (B, T, H, D) float32 or bfloat16 CUDA views (unit stride on D).
+    o: (B, T, H, D) contiguous; lse: (B, H, T) fp32; kbar/vbar: (B, H, Gc, D).
+    """
+    q, k, v = _prep(q, "q"), _prep(k, "k"), _prep(v, "v")
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError(f"q, k, v shapes differ: {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"q, k, v dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"sqrt_block_attention supports float32 and bfloat16, got {q.dtype}")
+    B, T, H, D = q.shape
+    b, G, Gc = _lib.geometry(T, block)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = q.device
+    o = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    lse = torch.empty((B, H, T), dtype=torch.float32, device=dev)
+    kbar = torch.empty((B, H, Gc, D), dtype=q.dtype, device=dev)
+    vbar = torch.empty((B, H, Gc, D), dtype=q.dtype, device=dev)
+    nbytes = _lib.workspace_bytes(B, T, H, D, b)
+    ws = _workspace(dev, nbytes)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    st = _lib.strides_array(_strides(q), _strides(k), _strides(v), _strides(o))
+    rc = _lib.lib().sqb_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                            lse.data_ptr(), kbar.data_ptr() if Gc else None,
+                            vbar.data_ptr() if Gc else None, B, T, H, D, b, st,
+                            _DTYPES[q.dtype], float(scale), _impl_code(impl), ws.data_ptr(),
+                            ws.numel(), stream)
+    _lib.check("sqb_fwd", rc)
+    return o, lse, kbar, vbar
+
+
+def sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block=None, scale=None,
+                        impl="auto"):
+    """Backward from saved forward outputs -> (dq, dk, dv), each (B, T, H, D)."""
+    q, k, v, o = _prep(q, "q"), _prep(k, "k"), _prep(v, "v"), _prep(o, "o")
+    dout = _prep(dout, "dout")
+    if dout.dtype != q.dtype:
+        dout = dout.to(q.dtype)
+    B, T, H, D = q.shape
+    b, G, Gc = _lib.geometry(T, block)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = q.device
+    dq = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    dk = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    dv = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    nbytes = _lib.workspace_bytes(B, T, H, D, b)
+    ws = _workspace(dev, nbytes)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    st = _lib.strides_array(*(_strides(t) for t in (q, k, v, o, dout, dq, dk, dv)))
+    lse = lse.contiguous()
+    rc = _lib.lib().sqb_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                            dout.data_ptr(), lse.data_ptr(),
+                            kbar.data_ptr() if Gc else None, vbar.data_ptr() if Gc else None,
+                            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, T, H, D, b, st,
+                            _DTYPES[q.dtype], float(scale), _impl_code(impl), ws.data_ptr(),
+                            ws.numel(), stream)
+    _lib.check("sqb_bwd", rc)
+    return dq, dk, dv
+
+
+def read_status(device=None) -> int:
+    """Synchronize and return (then clear) the device-side status of the workspace."""
+    dev = torch.device("cuda", device if isinstance(device, int) else
+                       (device.index if device is not None and device.index is not None
+                        else torch.cuda.current_device()))
+    ws = _workspaces.get(dev.index)
+    if ws is None:
+        return _lib.SQB_OK
+    detail = _lib.ctypes.c_int64()
+    return _lib.lib().sqb_read_status(ws.data_ptr(), torch.cuda.current_stream(dev).cuda_stream,
+                                      _lib.ctypes.byref(detail))
+
+
+class _SqrtBlockAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, block, scale, impl):
+        o, lse, kbar, vbar = sqrt_block_forward(q, k, v, block, scale, impl)
+        ctx.save_for_backward(q, k, v, o, lse, kbar, vbar)
+        ctx.cfg = (block, scale, impl)
+        return o
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, o, lse, kbar, vbar = ctx.saved_tensors
+        block, scale, impl = ctx.cfg
+        dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block, scale, impl)
+        return dq, dk, dv, None, None, None
+
+
+def sqrt_block_attention(q, k, v, block=None, scale=None, impl="auto"):
+    """Differentiable sqrt-block attention on (B, T, H, D) CUDA views -> O (B, T, H, D)."""
+    return _SqrtBlockAttention.apply(q, k, v, block, scale, impl)
