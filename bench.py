@@ -211,14 +211,25 @@ def run_ours(args, world, rank, local):
     host = make_inputs(args.seed, rank, dev)
     q, k, v, do = [x.to(dev) for x in host]
     block = 128
-    impl = args.kernels
-    if impl == "auto":
+    fwd_impl = bwd_impl = args.kernels
+    if args.kernels == "auto":
+        # the tcgen05 family where it has a kernel for this shape, else SIMT
+        qs, ks, vs, dos = q[:, :256], k[:, :256], v[:, :256], do[:, :256]
         try:
-            sqrt_block_forward(q[:, :256], k[:, :256], v[:, :256], block, None, "tcgen05")
-            impl = "tcgen05"
+            o_, l_, kb_, vb_ = sqrt_block_forward(qs, ks, vs, block, None, "tcgen05")
+            fwd_impl = "tcgen05"
         except _lib.SqrtBlockError:
-            impl = "simt"
-    launches_per_step = {"tcgen05": 2, "simt": 7}[impl]
+            o_, l_, kb_, vb_ = sqrt_block_forward(qs, ks, vs, block, None, "simt")
+            fwd_impl = "simt"
+        try:
+            sqrt_block_backward(qs, ks, vs, o_, l_, kb_, vb_, dos, block, None, "tcgen05")
+            bwd_impl = "tcgen05"
+        except _lib.SqrtBlockError:
+            bwd_impl = "simt"
+    # kernels each call launches: tcgen05 fwd 1, bwd 1; SIMT fwd 2 (pool,
+    # attention), bwd 4 (delta, summary gradients, dQ, dK/dV)
+    launches_per_step = {"tcgen05": 1, "simt": 2}[fwd_impl] + {"tcgen05": 1, "simt": 4}[bwd_impl]
+    impl = f"fwd:{fwd_impl},bwd:{bwd_impl}"
 
     stream = torch.cuda.current_stream(dev)
     f_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
@@ -227,11 +238,11 @@ def run_ours(args, world, rank, local):
     def step(i=None):
         if i is not None:
             f_ev[2 * i].record(stream)
-        o, lse, kbar, vbar = sqrt_block_forward(q, k, v, block, None, impl)
+        o, lse, kbar, vbar = sqrt_block_forward(q, k, v, block, None, fwd_impl)
         if i is not None:
             f_ev[2 * i + 1].record(stream)
             b_ev[2 * i].record(stream)
-        dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, do, block, None, impl)
+        dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, do, block, None, bwd_impl)
         if i is not None:
             b_ev[2 * i + 1].record(stream)
         return o, dq
@@ -266,7 +277,7 @@ def run_ours(args, world, rank, local):
         qd, kd, vd, dod = [x.to(dev, non_blocking=True) for x in pinned]
         for t in (qd, kd, vd):
             t.requires_grad_(True)
-        o = sqrt_block_attention(qd, kd, vd, block, None, impl)
+        o = sqrt_block_attention(qd, kd, vd, block, None, "auto")
         o.backward(dod)
         for dst, src in zip(outs, (o.detach(), qd.grad, kd.grad, vd.grad)):
             dst.copy_(src, non_blocking=True)
@@ -301,7 +312,7 @@ def run_ours(args, world, rank, local):
     traffic_path = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(traffic_path):
         try:
-            roofline["traffic"] = json.load(open(traffic_path)).get(impl, {}).get(dom[0])
+            roofline["traffic"] = json.load(open(traffic_path)).get(dom[0])
         except Exception:
             pass
 

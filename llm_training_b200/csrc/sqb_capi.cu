@@ -113,7 +113,7 @@ int sqb_fwd(const void* q, const void* k, const void* v, void* o, float* lse, vo
              to = view(o, strides + 9);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaGetLastError();  // clear a stale error so launch checks see only ours
-  const bool tc_ok = sm100_supported(p, {tq, tk, tv, to}, lse, kbar, vbar);
+  const bool tc_ok = sm100_fwd_supported(p, {tq, tk, tv, to}, lse, kbar, vbar);
   if (impl == SQB_IMPL_TCGEN05 && !tc_ok) return SQB_ERR_UNSUPPORTED;
   if (impl == SQB_IMPL_TCGEN05 || (impl == SQB_IMPL_AUTO && tc_ok))
     return sm100_forward(p, tq, tk, tv, to, lse, kbar, vbar, (uint8_t*)workspace, wl, s);
@@ -142,7 +142,8 @@ int sqb_bwd(const void* q, const void* k, const void* v, const void* o, const vo
              tdv = view(dv, strides + 21);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaGetLastError();
-  const bool tc_ok = sm100_supported(p, {tq, tk, tv, to, tdo, tdq, tdk, tdv}, lse, kbar, vbar);
+  const bool tc_ok =
+      sm100_bwd_supported(p, {tq, tk, tv, to, tdo, tdq, tdk, tdv}, lse, kbar, vbar);
   if (impl == SQB_IMPL_TCGEN05 && !tc_ok) return SQB_ERR_UNSUPPORTED;
   if (impl == SQB_IMPL_TCGEN05 || (impl == SQB_IMPL_AUTO && tc_ok))
     return sm100_backward(p, tq, tk, tv, to, tdo, lse, kbar, vbar, tdq, tdk, tdv,

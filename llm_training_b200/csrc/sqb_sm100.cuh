@@ -2,6 +2,8 @@
 // TMEM accumulators, operands staged in shared memory by TMA (no multicast).
 #pragma once
 
+#include <cuda.h>
+
 #include <initializer_list>
 
 #include "sqb_internal.cuh"
@@ -9,10 +11,12 @@
 namespace sqb {
 
 // True when the tcgen05 kernels handle this problem and these tensor views
-// (bf16, supported D and block length, 16-byte aligned pointers and strides,
-// sm_100-class device).
-bool sm100_supported(const Problem& p, std::initializer_list<TensorView> views, const float* lse,
-                     const void* kbar, const void* vbar);
+// (bf16, D in {64, 128}, block length a multiple of 16 in [32, 128], 16-byte
+// aligned pointers and strides, sm_100-class device).
+bool sm100_fwd_supported(const Problem& p, std::initializer_list<TensorView> views,
+                         const float* lse, const void* kbar, const void* vbar);
+bool sm100_bwd_supported(const Problem& p, std::initializer_list<TensorView> views,
+                         const float* lse, const void* kbar, const void* vbar);
 
 int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,
                   float* lse, void* kbar, void* vbar, uint8_t* ws, const WorkspaceLayout& wl,
@@ -23,4 +27,17 @@ int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, T
                    TensorView dq, TensorView dk, TensorView dv, uint8_t* ws,
                    const WorkspaceLayout& wl, cudaStream_t stream);
 
+namespace sm100 {
+
+// Rows per work tile: 128 when b divides 128 (whole blocks per tile), else b.
+inline int tile_rows(int b) { return (128 % b == 0) ? 128 : b; }
+
+struct TensorMaps {
+  CUtensorMap q, k, v, o, kbar, vbar;
+};
+
+int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
+                   uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream);
+
+}  // namespace sm100
 }  // namespace sqb

@@ -1,0 +1,92 @@
+// Shared definitions of the sm_100a forward and backward kernels: tile geometry,
+// kernel parameters and the shared-memory swizzle used by every operand tile.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "sqb_internal.cuh"
+#include "sqb_ptx.cuh"
+
+namespace sqb {
+namespace sm100 {
+
+constexpr int kTileRows = 128;    // TMEM lanes / UMMA M
+constexpr int kAtomCols = 64;     // bf16 columns per 128-byte swizzle atom
+constexpr int kAtomBytes = kTileRows * 128;  // one 64-column atom of a 128-row tile
+
+// Work tile: a run of R query rows that starts on a block boundary and holds
+// whole blocks (R = 128 when b divides 128, else R = b, one block per tile).
+// Tiles of one (batch, head) sequence are numbered s = 0 .. tiles_per_seq-1.
+struct Geometry {
+  int T, b, Gc, R, tiles_per_seq;
+};
+
+struct Tile {
+  int s, bh, n, h;  // sequence tile, batch*head, batch, head
+  int r0, rows;     // first row, valid rows (<= R)
+  int blk0;         // first block of the tile
+  int ns;           // summaries the last row sees: min(last block, Gc)
+  int nsc;          // summary chunks of <= 128 summaries
+  int n_in;         // MMA N of the in-block chunk (rows rounded up to 16)
+};
+
+__host__ __device__ inline int round16(int x) { return (x + 15) & ~15; }
+
+__device__ inline Tile make_tile(const Geometry& g, int H, int s, int bh) {
+  Tile t;
+  t.s = s;
+  t.bh = bh;
+  t.n = bh / H;
+  t.h = bh % H;
+  t.r0 = s * g.R;
+  t.rows = min(g.R, g.T - t.r0);
+  t.blk0 = t.r0 / g.b;
+  const int last_blk = (t.r0 + t.rows - 1) / g.b;
+  t.ns = min(last_blk, g.Gc);
+  t.nsc = (t.ns + 127) / 128;
+  t.n_in = round16(t.rows);
+  return t;
+}
+
+// Summary chunk c (0-based) covers summaries [128c, e); the 16-row-rounded MMA
+// width N16 is loaded from window start w = e - N16 so that every row the MMA
+// reads is either an earlier, already-published summary or out of bounds
+// (zero-filled by TMA), never an unpublished one.
+struct SumChunk {
+  int lo, e, n16, w;
+};
+
+__device__ inline SumChunk sum_chunk(const Tile& t, int c) {
+  SumChunk k;
+  k.lo = 128 * c;
+  k.e = min(128 * (c + 1), t.ns);
+  k.n16 = round16(k.e - k.lo);
+  k.w = k.e - k.n16;
+  return k;
+}
+
+// Byte offset of element (row, col) in a 128-row tile stored as 64-column
+// atoms of 128-byte rows with the 128B swizzle (16-byte chunk ^= row % 8), the
+// layout TMA writes for a box of (64, rows) with CU_TENSOR_MAP_SWIZZLE_128B.
+__device__ __forceinline__ uint32_t swz_offset(int row, int col) {
+  const int atom = col >> 6;
+  const int chunk = (col >> 3) & 7;
+  return atom * kAtomBytes + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
+}
+
+// UMMA descriptors over such tiles.
+// K-major operand (rows = M or N, K along the 64-column atoms): k-step kk of
+// 16 elements starts at atom kk/4, byte 32*(kk%4) of each row; SBO = 8 rows.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile_saddr, int kk) {
+  return ptx::smem_desc_sw128(tile_saddr + (kk >> 2) * kAtomBytes + (kk & 3) * 32, 16, 1024);
+}
+// MN-major operand (rows = K, 64-column atoms along N): k-step kk covers rows
+// 16kk..16kk+15; LBO = next 64-column atom, SBO = next 8 rows.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile_saddr, int kk) {
+  return ptx::smem_desc_sw128(tile_saddr + kk * 16 * 128, kAtomBytes, 1024);
+}
+
+}  // namespace sm100
+}  // namespace sqb

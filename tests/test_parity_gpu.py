@@ -36,13 +36,28 @@ def to_np(x):
 
 
 def run(q, k, v, do, block, impl):
+    """Forward and backward with the requested kernel family.  Where the
+    tcgen05 family has no kernel for one direction, that direction runs with
+    "auto"; if it has neither, the test is skipped."""
+    used = []
     try:
         o, lse, kbar, vbar = sqrt_block_forward(q, k, v, block, None, impl)
+        used.append(impl)
     except _lib.SqrtBlockError as e:
-        if e.code == 4 and impl == "tcgen05":
-            pytest.skip("tcgen05 kernels do not cover this case")
-        raise
-    dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, do, block, None, impl)
+        if e.code != 4 or impl != "tcgen05":
+            raise
+        o, lse, kbar, vbar = sqrt_block_forward(q, k, v, block, None, "auto")
+        used.append("auto")
+    try:
+        dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, do, block, None, impl)
+        used.append(impl)
+    except _lib.SqrtBlockError as e:
+        if e.code != 4 or impl != "tcgen05":
+            raise
+        dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, do, block, None, "auto")
+        used.append("auto")
+    if impl == "tcgen05" and used == ["auto", "auto"]:
+        pytest.skip("tcgen05 kernels do not cover this case")
     torch.cuda.synchronize()
     assert read_status() == 0
     return o, lse, dq, dk, dv
