@@ -247,13 +247,20 @@ def run_ours(args, world, rank, local):
             b_ev[2 * i + 1].record(stream)
         return o, dq
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        # warm up for at least W steps and ~0.5 s so the clock sampler (100 ms
+        # period) has samples under load when the timed region starts
+        t_end = time.perf_counter() + 0.5
+        i = 0
+        while i < max(args.warmup, 3) or time.perf_counter() < t_end:
+            step()
+            i += 1
+            if i % 16 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for i in range(args.steps):
             step(i)
@@ -349,7 +356,7 @@ def run_ours(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--kernels", choices=["auto", "tcgen05", "simt"], default="auto")

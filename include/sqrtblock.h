@@ -31,9 +31,12 @@
  *   - Return value: SQB_OK, or an SQB_ERR_* code for a rejected argument or a
  *     failed launch.  Device-side failures (a bounded wait that gave up) are
  *     recorded in the workspace and read back by sqb_read_status.
- *   - The workspace must be zero-filled once before its first use and then
- *     passed unchanged to later calls; calls sharing a workspace must be
- *     ordered on one stream.  After any device-side error, zero it again.
+ *   - The workspace belongs to one problem shape (B, T, H, D, block): it
+ *     must be zero-filled once before its first use and then passed
+ *     unchanged to later calls with that shape (its regions are laid out per
+ *     shape and the kernels leave them clean for the next call).  Calls
+ *     sharing a workspace must be ordered on one stream.  After any
+ *     device-side error, zero it again.
  */
 #ifndef SQRTBLOCK_H_
 #define SQRTBLOCK_H_

@@ -1,0 +1,493 @@
+// sm_100a backward kernel of sqrt-block attention.
+//
+// Persistent, warp-specialised, one CTA per SM (192 threads):
+//   warp 0      TMA producer + tile scheduler
+//   warp 1      tcgen05.mma issuer and TMEM owner
+//   warps 2-5   softmax-gradient / epilogue, one TMEM lane per thread
+//
+// A work tile is the same R-row tile as in the forward.  Its chunks are the
+// summary chunks first, then the tile's own (in-block) keys.  Per chunk, with
+// LSE and delta = rowsum(dO * O) per query row:
+//   S  = Q Kc^T, dP = dO Vc^T                       (TMEM, lanes = queries)
+//   P  = exp2(S*c - LSE*log2e), dS = scale * P * (dP - delta)  -> smem (bf16)
+//   dVc = P^T dO, dKc = dS^T Q                       (TMEM, lanes = keys)
+//   dQ += dS Kc                                      (TMEM, lanes = queries)
+// For a summary chunk, dKc/dVc are summary gradients: they are added with
+// fp32 vector atomics into per-(batch, head) accumulators in the workspace.
+// For the in-block chunk they are the tile's own dK/dV, to which the epilogue
+// adds (summary gradient of the key's block) / b - a summary is the mean of
+// its block - before storing dK, dV and dQ through smem with TMA.
+//
+// The summary gradient of block j is complete once every later tile has
+// added to it.  Tiles are handed out in descending sequence order; each tile
+// sets flag[s] once its own additions are done, and before reading its blocks'
+// sums checks (32 flags at a time) that every later tile has set its flag.
+// The reader re-zeroes the sums it consumed, so the accumulators are zero
+// again when the kernel ends.  Waits are bounded like the forward's.
+
+#include "sqb_sm100.cuh"
+#include "sqb_sm100_common.cuh"
+
+namespace sqb {
+namespace sm100 {
+namespace {
+
+struct BwdParams {
+  Geometry g;
+  int H, BH;
+  int total_tiles;
+  float scale;       // softmax scale, folded into dS
+  float scale_log2;  // scale * log2(e)
+  const float* lse;
+  const __nv_bfloat16* o;
+  int64_t o_sb, o_st, o_sh;
+  float* dkbar;  // fp32 (BH, Gc, D) accumulators, zero between launches
+  float* dvbar;
+  uint32_t* ctrl;
+  uint32_t* flags;
+  int flags_stride;
+};
+
+template <int D>
+struct BwdSmem {
+  static constexpr int kTileBytes = (D / 64) * kAtomBytes;
+  alignas(1024) uint8_t q[kTileBytes];     // Q, then dQ staging
+  alignas(1024) uint8_t dout[kTileBytes];  // dO
+  alignas(1024) uint8_t k[kTileBytes];     // K chunk, then dK staging
+  alignas(1024) uint8_t v[kTileBytes];     // V chunk, then dV staging
+  alignas(1024) uint8_t p[2 * kAtomBytes];   // P  (128 query rows x 128 key cols)
+  alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout)
+  uint64_t ld_full, q_empty, kv_full, kv_empty, s_full, ps_full, g_full, g_free;
+  int tile_ring;
+  uint32_t tmem_base;
+};
+
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// TMEM columns: S / dV chunk at 0, dP / dK chunk at 128, dQ at 256.
+constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+               const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
+               const __grid_constant__ CUtensorMap tm_dv,
+               const __grid_constant__ CUtensorMap tm_kbar,
+               const __grid_constant__ CUtensorMap tm_vbar, const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  BwdSmem<D>& sm = *reinterpret_cast<BwdSmem<D>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint32_t* status = p.ctrl + kStatus;
+  const uint32_t token = *reinterpret_cast<volatile uint32_t*>(p.ctrl + kBwdEpoch) + 1u;
+  constexpr int kAtoms = D / 64;
+  const uint32_t box_bytes = (uint32_t)p.g.R * 128u;
+  const int NT = p.g.tiles_per_seq;
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&sm.ld_full, 1);
+    ptx::mbar_init(&sm.q_empty, 1);
+    ptx::mbar_init(&sm.kv_full, 1);
+    ptx::mbar_init(&sm.kv_empty, 1);
+    ptx::mbar_init(&sm.s_full, 1);
+    ptx::mbar_init(&sm.ps_full, 4);
+    ptx::mbar_init(&sm.g_full, 1);
+    ptx::mbar_init(&sm.g_free, 4);
+    ptx::fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::tma_prefetch_desc(&tm_q);
+    ptx::tma_prefetch_desc(&tm_do);
+    ptx::tma_prefetch_desc(&tm_k);
+    ptx::tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(&sm.tmem_base, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  auto tile_of = [&](int n) {
+    return make_tile(p.g, p.H, NT - 1 - n / p.BH, n % p.BH);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int tc = 0, kc = 0;
+      while (true) {
+        int n = (int)atomicAdd(p.ctrl + kBwdTileCounter, 1u);
+        if (n >= p.total_tiles) n = -1;
+        ptx::mbar_wait(&sm.q_empty, (tc & 1) ^ 1, status, 0x50000000u);
+        sm.tile_ring = n;
+        if (n < 0) {
+          ptx::mbar_arrive(&sm.ld_full);
+          break;
+        }
+        const Tile t = tile_of(n);
+        ptx::mbar_arrive_expect_tx(&sm.ld_full, 2 * kAtoms * box_bytes);
+#pragma unroll
+        for (int a = 0; a < kAtoms; ++a) {
+          ptx::tma_load_4d(sm.q + a * kAtomBytes, &tm_q, &sm.ld_full, a * 64, t.h, t.r0, t.n);
+          ptx::tma_load_4d(sm.dout + a * kAtomBytes, &tm_do, &sm.ld_full, a * 64, t.h, t.r0,
+                           t.n);
+        }
+        for (int c = 0; c <= t.nsc; ++c) {
+          ptx::mbar_wait(&sm.kv_empty, (kc & 1) ^ 1, status, 0x51000000u);
+          if (c < t.nsc) {
+            const SumChunk sc = sum_chunk(t, c);
+            ptx::mbar_arrive_expect_tx(&sm.kv_full, 2 * kAtoms * kAtomBytes);
+#pragma unroll
+            for (int a = 0; a < kAtoms; ++a) {
+              ptx::tma_load_3d(sm.k + a * kAtomBytes, &tm_kbar, &sm.kv_full, a * 64, sc.w, t.bh);
+              ptx::tma_load_3d(sm.v + a * kAtomBytes, &tm_vbar, &sm.kv_full, a * 64, sc.w, t.bh);
+            }
+          } else {
+            ptx::mbar_arrive_expect_tx(&sm.kv_full, 2 * kAtoms * box_bytes);
+#pragma unroll
+            for (int a = 0; a < kAtoms; ++a) {
+              ptx::tma_load_4d(sm.k + a * kAtomBytes, &tm_k, &sm.kv_full, a * 64, t.h, t.r0, t.n);
+              ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_v, &sm.kv_full, a * 64, t.h, t.r0, t.n);
+            }
+          }
+          ++kc;
+        }
+        ++tc;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_dvdk = ptx::idesc_bf16(128, D, true, true);
+      const uint32_t idesc_dq = ptx::idesc_bf16(128, D, false, true);
+      const uint32_t q_s = ptx::smem_u32(sm.q), do_s = ptx::smem_u32(sm.dout);
+      const uint32_t k_s = ptx::smem_u32(sm.k), v_s = ptx::smem_u32(sm.v);
+      const uint32_t p_s = ptx::smem_u32(sm.p), ds_s = ptx::smem_u32(sm.ds);
+      int tc = 0, kc = 0;
+      while (true) {
+        ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x60000000u);
+        const int n = sm.tile_ring;
+        if (n < 0) break;
+        const Tile t = tile_of(n);
+        const int kq = round16(t.rows) / 16;  // k-steps over query rows
+        for (int c = 0; c <= t.nsc; ++c) {
+          const int N = c < t.nsc ? sum_chunk(t, c).n16 : t.n_in;
+          ptx::mbar_wait(&sm.kv_full, kc & 1, status, 0x61000000u);
+          if (kc > 0) ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
+          ptx::tc_fence_after();
+          const uint32_t idesc_s = ptx::idesc_bf16(128, N, false, false);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            ptx::mma_ss(tmem + kColS, desc_kmajor(q_s, kk), desc_kmajor(k_s, kk), idesc_s,
+                        kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            ptx::mma_ss(tmem + kColDP, desc_kmajor(do_s, kk), desc_kmajor(v_s, kk), idesc_s,
+                        kk > 0 ? 1u : 0u);
+          ptx::mma_commit(&sm.s_full);
+          ptx::mbar_wait(&sm.ps_full, kc & 1, status, 0x63000000u);
+          ptx::tc_fence_after();
+          for (int kk = 0; kk < kq; ++kk)  // dVc = P^T dO
+            ptx::mma_ss(tmem + kColS, desc_mnmajor(p_s, kk), desc_mnmajor(do_s, kk), idesc_dvdk,
+                        kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kq; ++kk)  // dKc = dS^T Q
+            ptx::mma_ss(tmem + kColDP, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
+                        kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < N / 16; ++kk)  // dQ += dS Kc
+            ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
+                        (c > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_commit(&sm.g_full);
+          ++kc;
+        }
+        ++tc;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ gradient warps
+    const int stid = threadIdx.x - 64;  // 0..127
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane: query row, then key row
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float inv_b = 1.f / (float)p.g.b;
+    int tc = 0, kc = 0;
+    while (true) {
+      ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x70000000u);
+      const int n = sm.tile_ring;
+      if (n < 0) break;
+      const Tile t = tile_of(n);
+      const bool valid = row < t.rows;
+      const int tq = t.r0 + row;
+      const int blk_t = valid ? tq / p.g.b : 0;
+      const int lim = valid ? min(blk_t, p.g.Gc) : 0;
+      const float L = valid ? p.lse[(size_t)t.bh * p.g.T + tq] * kLog2e : 0.f;
+      float delta = 0.f;
+      if (valid) {
+        const uint4* orow = reinterpret_cast<const uint4*>(
+            p.o + t.n * p.o_sb + (int64_t)tq * p.o_st + t.h * p.o_sh);
+#pragma unroll 4
+        for (int cc = 0; cc < D / 8; ++cc) {
+          const uint4 a = orow[cc];
+          const uint4 g = *reinterpret_cast<const uint4*>(sm.dout + swz_offset(row, cc * 8));
+          delta += bf16lo(a.x) * bf16lo(g.x) + bf16hi(a.x) * bf16hi(g.x) +
+                   bf16lo(a.y) * bf16lo(g.y) + bf16hi(a.y) * bf16hi(g.y) +
+                   bf16lo(a.z) * bf16lo(g.z) + bf16hi(a.z) * bf16hi(g.z) +
+                   bf16lo(a.w) * bf16lo(g.w) + bf16hi(a.w) * bf16hi(g.w);
+        }
+      }
+
+      // P and dS of one chunk into smem (all 128 key columns; masked -> 0)
+      auto softmax_grad = [&](int N, int vlo, int vhi) {
+        ptx::mbar_wait(&sm.s_full, kc & 1, status, 0x71000000u);
+        ptx::tc_fence_after();
+#pragma unroll 1
+        for (int pc = 0; pc < 4; ++pc) {
+          uint32_t s[32], dp[32];
+          const bool live = pc * 32 < N;  // warp-uniform
+          if (live) {
+            ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, s);
+            ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, dp);
+            ptx::tmem_wait_ld();
+          }
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            uint32_t pw[4], dw[4];
+#pragma unroll
+            for (int h2 = 0; h2 < 4; ++h2) {
+              float pv[2], dv[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int j = j8 * 8 + h2 * 2 + e;
+                const int col = pc * 32 + j;
+                const bool ok = live && col >= vlo && col < vhi;
+                const float pr = ok ? ptx::ex2(fmaf(__uint_as_float(s[j]), p.scale_log2, -L))
+                                    : 0.f;
+                pv[e] = pr;
+                dv[e] = ok ? pr * (__uint_as_float(dp[j]) - delta) * p.scale : 0.f;
+              }
+              pw[h2] = ptx::pack_bf16x2(pv[0], pv[1]);
+              dw[h2] = ptx::pack_bf16x2(dv[0], dv[1]);
+            }
+            const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
+            *reinterpret_cast<uint4*>(sm.p + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+            *reinterpret_cast<uint4*>(sm.ds + off) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
+          }
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&sm.ps_full);
+        ptx::mbar_wait(&sm.g_full, kc & 1, status, 0x72000000u);
+        ptx::tc_fence_after();
+      };
+
+      // ---- summary chunks: add dKc / dVc to the summary accumulators
+      for (int c = 0; c < t.nsc; ++c) {
+        const SumChunk sc = sum_chunk(t, c);
+        softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
+        const int j = sc.w + row;  // this lane's summary
+        const bool ok = row >= sc.lo - sc.w && row < sc.e - sc.w;
+        float* dkrow = p.dkbar + ((size_t)t.bh * p.g.Gc + j) * D;
+        float* dvrow = p.dvbar + ((size_t)t.bh * p.g.Gc + j) * D;
+#pragma unroll 1
+        for (int pc = 0; pc < D / 32; ++pc) {
+          uint32_t gv[32], gk[32];
+          ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, gv);
+          ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, gk);
+          ptx::tmem_wait_ld();
+          if (ok) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              atomicAdd(reinterpret_cast<float4*>(dvrow + pc * 32 + 4 * j4),
+                        make_float4(__uint_as_float(gv[4 * j4]), __uint_as_float(gv[4 * j4 + 1]),
+                                    __uint_as_float(gv[4 * j4 + 2]),
+                                    __uint_as_float(gv[4 * j4 + 3])));
+              atomicAdd(reinterpret_cast<float4*>(dkrow + pc * 32 + 4 * j4),
+                        make_float4(__uint_as_float(gk[4 * j4]), __uint_as_float(gk[4 * j4 + 1]),
+                                    __uint_as_float(gk[4 * j4 + 2]),
+                                    __uint_as_float(gk[4 * j4 + 3])));
+            }
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+        if (stid == 0) ptx::mbar_arrive(&sm.kv_empty);
+        ++kc;
+      }
+
+      // ---- this tile's additions are done: publish
+      __threadfence();
+      ptx::named_barrier(1, 128);
+      if (stid == 0)
+        ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
+
+      // ---- in-block chunk, then the epilogue
+      softmax_grad(t.n_in, valid ? blk_t * p.g.b - t.r0 : 0, valid ? row + 1 : 0);
+      // every later tile of this sequence has added to the summary sums
+      if (stid < 32)
+        ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT, token,
+                              status, (uint32_t)n);
+      ptx::named_barrier(1, 128);
+      {
+        const bool complete = valid && blk_t < p.g.Gc;  // this lane's key is in a full block
+        const float* skrow = p.dkbar + ((size_t)t.bh * p.g.Gc + blk_t) * D;
+        const float* svrow = p.dvbar + ((size_t)t.bh * p.g.Gc + blk_t) * D;
+#pragma unroll 1
+        for (int pc = 0; pc < D / 32; ++pc) {
+          uint32_t gv[32], gk[32];
+          ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, gv);
+          ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, gk);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            float fk[8], fv[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              fk[e] = __uint_as_float(gk[8 * j8 + e]);
+              fv[e] = __uint_as_float(gv[8 * j8 + e]);
+            }
+            if (complete) {
+              const int col = pc * 32 + j8 * 8;
+              const float4 k0 = __ldcg(reinterpret_cast<const float4*>(skrow + col));
+              const float4 k1 = __ldcg(reinterpret_cast<const float4*>(skrow + col + 4));
+              const float4 v0 = __ldcg(reinterpret_cast<const float4*>(svrow + col));
+              const float4 v1 = __ldcg(reinterpret_cast<const float4*>(svrow + col + 4));
+              fk[0] += k0.x * inv_b; fk[1] += k0.y * inv_b; fk[2] += k0.z * inv_b;
+              fk[3] += k0.w * inv_b; fk[4] += k1.x * inv_b; fk[5] += k1.y * inv_b;
+              fk[6] += k1.z * inv_b; fk[7] += k1.w * inv_b;
+              fv[0] += v0.x * inv_b; fv[1] += v0.y * inv_b; fv[2] += v0.z * inv_b;
+              fv[3] += v0.w * inv_b; fv[4] += v1.x * inv_b; fv[5] += v1.y * inv_b;
+              fv[6] += v1.z * inv_b; fv[7] += v1.w * inv_b;
+            }
+            const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
+            *reinterpret_cast<uint4*>(sm.k + off) =
+                make_uint4(ptx::pack_bf16x2(fk[0], fk[1]), ptx::pack_bf16x2(fk[2], fk[3]),
+                           ptx::pack_bf16x2(fk[4], fk[5]), ptx::pack_bf16x2(fk[6], fk[7]));
+            *reinterpret_cast<uint4*>(sm.v + off) =
+                make_uint4(ptx::pack_bf16x2(fv[0], fv[1]), ptx::pack_bf16x2(fv[2], fv[3]),
+                           ptx::pack_bf16x2(fv[4], fv[5]), ptx::pack_bf16x2(fv[6], fv[7]));
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+#pragma unroll 1
+        for (int pc = 0; pc < D / 32; ++pc) {
+          uint32_t gq[32];
+          ptx::tmem_ld32(tmem + lane_off + kColDQ + pc * 32, gq);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
+            *reinterpret_cast<uint4*>(sm.q + off) = make_uint4(
+                ptx::pack_bf16x2(__uint_as_float(gq[8 * j8]), __uint_as_float(gq[8 * j8 + 1])),
+                ptx::pack_bf16x2(__uint_as_float(gq[8 * j8 + 2]), __uint_as_float(gq[8 * j8 + 3])),
+                ptx::pack_bf16x2(__uint_as_float(gq[8 * j8 + 4]), __uint_as_float(gq[8 * j8 + 5])),
+                ptx::pack_bf16x2(__uint_as_float(gq[8 * j8 + 6]),
+                                 __uint_as_float(gq[8 * j8 + 7])));
+          }
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::named_barrier(1, 128);
+        // re-zero the summary sums this tile consumed (all later adders are done)
+        const int nb = p.g.R / p.g.b;
+        const int nfull = max(0, min(nb, p.g.Gc - t.blk0));
+        for (int lb = 0; lb < nfull; ++lb) {
+          const size_t base = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D;
+          for (int i = stid; i < D; i += 128) {
+            p.dkbar[base + i] = 0.f;
+            p.dvbar[base + i] = 0.f;
+          }
+        }
+        if (stid == 0) {
+#pragma unroll
+          for (int a = 0; a < kAtoms; ++a) {
+            ptx::tma_store_4d(&tm_dk, sm.k + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+            ptx::tma_store_4d(&tm_dv, sm.v + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+            ptx::tma_store_4d(&tm_dq, sm.q + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+          }
+          ptx::tma_store_commit();
+          ptx::tma_store_wait_read_all();
+          ptx::mbar_arrive(&sm.kv_empty);
+          ptx::mbar_arrive(&sm.q_empty);
+        }
+        ++kc;
+      }
+      ++tc;
+    }
+    if (stid == 0) ptx::tma_store_wait_all();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.ctrl + kBwdExitCounter, 1u);
+    if (prev == gridDim.x - 1) {
+      atomicExch(p.ctrl + kBwdTileCounter, 0u);
+      atomicExch(p.ctrl + kBwdExitCounter, 0u);
+      __threadfence();
+      atomicExch(p.ctrl + kBwdEpoch, token);
+    }
+  }
+}
+
+template <int D>
+int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
+           uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
+  BwdParams p;
+  p.g.T = pr.T;
+  p.g.b = pr.b;
+  p.g.Gc = pr.Gc;
+  p.g.R = tile_rows(pr.b);
+  p.g.tiles_per_seq = (pr.T + p.g.R - 1) / p.g.R;
+  p.H = pr.H;
+  p.BH = pr.B * pr.H;
+  p.total_tiles = p.g.tiles_per_seq * p.BH;
+  p.scale = pr.scale;
+  p.scale_log2 = pr.scale * kLog2e;
+  p.lse = lse;
+  p.o = reinterpret_cast<const __nv_bfloat16*>(o.ptr);
+  p.o_sb = o.sb;
+  p.o_st = o.st;
+  p.o_sh = o.sh;
+  p.dkbar = reinterpret_cast<float*>(ws + wl.dkbar);
+  p.dvbar = reinterpret_cast<float*>(ws + wl.dvbar);
+  p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
+  p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_bwd);
+  p.flags_stride = wl.tiles_per_seq;
+  const size_t smem = sizeof(BwdSmem<D>) + 1024;
+  if (cudaFuncSetAttribute(bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return SQB_ERR_LAUNCH;
+  const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
+  bwd_kernel<D><<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.dout, tm.dq, tm.dk, tm.dv,
+                                                   tm.kbar, tm.vbar, p);
+  return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
+}
+
+}  // namespace
+
+int launch_backward(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
+                    uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
+  if (pr.D == 64) return launch<64>(pr, tm, lse, o, ws, wl, num_sms, stream);
+  if (pr.D == 128) return launch<128>(pr, tm, lse, o, ws, wl, num_sms, stream);
+  return SQB_ERR_UNSUPPORTED;
+}
+
+}  // namespace sm100
+}  // namespace sqb

@@ -18,9 +18,9 @@
 //
 // Summaries cross CTAs: tiles are handed out in ascending sequence order
 // (tile index n -> s = n / BH), the pooling warps of tile s publish their
-// blocks' means, then wait for flag[s-1] and set flag[s] (a chain: flag[s]
-// means every tile <= s has published).  The producer of a tile waits for the
-// chain flag covering the summaries it needs before loading them with TMA.
+// blocks' means and set flag[s].  Before loading summaries with TMA the
+// producer warp checks, 32 flags at a time, that every tile holding one of
+// the summaries it needs has published.
 // A tile only ever waits on tiles with a smaller index, and tiles are only
 // claimed by running CTAs, so every wait ends; each is still bounded in time
 // and records SQB_ERR_TIMEOUT if it gives up.  Flags carry an epoch token so
@@ -119,27 +119,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int tc = 0, kc = 0;
-      while (true) {
-        const int slot = tc & 1;
-        int n = (int)atomicAdd(p.ctrl + kFwdTileCounter, 1u);
+    // The whole warp runs the loop (the summary-flag wait is warp-parallel);
+    // lane 0 claims tiles and issues every TMA and barrier operation.
+    int tc = 0, kc = 0;
+    while (true) {
+      const int slot = tc & 1;
+      int n = 0;
+      if (lane == 0) {
+        n = (int)atomicAdd(p.ctrl + kFwdTileCounter, 1u);
         if (n >= p.total_tiles) n = -1;
-        ptx::mbar_wait(&sm.q_empty[slot], ((tc >> 1) & 1) ^ 1, status, 0x10000000u | slot);
+      }
+      n = __shfl_sync(0xffffffffu, n, 0);
+      ptx::mbar_wait(&sm.q_empty[slot], ((tc >> 1) & 1) ^ 1, status, 0x10000000u | slot);
+      if (lane == 0) {
         sm.tile_ring[slot] = n;
-        if (n < 0) {
-          ptx::mbar_arrive(&sm.q_full[slot]);
-          break;
-        }
-        const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
+        if (n < 0) ptx::mbar_arrive(&sm.q_full[slot]);
+      }
+      if (n < 0) break;
+      const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
+      if (lane == 0) {
         ptx::mbar_arrive_expect_tx(&sm.q_full[slot], kAtoms * box_bytes);
 #pragma unroll
         for (int a = 0; a < kAtoms; ++a)
           ptx::tma_load_4d(sm.q[slot] + a * kAtomBytes, &tm_q, &sm.q_full[slot], a * 64, t.h,
                            t.r0, t.n);
-        {
-          const int st = kc & 1;
-          ptx::mbar_wait(&sm.kv_empty[st], ((kc >> 1) & 1) ^ 1, status, 0x11000000u | st);
+      }
+      {
+        const int st = kc & 1;
+        ptx::mbar_wait(&sm.kv_empty[st], ((kc >> 1) & 1) ^ 1, status, 0x11000000u | st);
+        if (lane == 0) {
           ptx::mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kAtoms * box_bytes);
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a) {
@@ -148,30 +156,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tma_load_4d(sm.v[st] + a * kAtomBytes, &tm_v, &sm.kv_full[st], a * 64, t.h,
                              t.r0, t.n);
           }
-          ++kc;
         }
-        if (t.nsc > 0) {
-          const int s_need = ((t.ns - 1) * p.g.b) / p.g.R;
-          ptx::flag_wait(p.flags + (size_t)t.bh * p.flags_stride + s_need, token, status,
-                         (uint32_t)n);
-          ptx::fence_proxy_async_global();
-          for (int c = 0; c < t.nsc; ++c) {
-            const SumChunk sc = sum_chunk(t, c);
-            const int st = kc & 1;
-            ptx::mbar_wait(&sm.kv_empty[st], ((kc >> 1) & 1) ^ 1, status, 0x12000000u | st);
+        ++kc;
+      }
+      if (t.nsc > 0) {
+        // every tile holding one of the needed summaries has published
+        const int s_need = ((t.ns - 1) * p.g.b) / p.g.R;
+        ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, 0, s_need + 1, token,
+                              status, (uint32_t)n);
+        if (lane == 0) ptx::fence_proxy_async_global();
+        for (int c = 0; c < t.nsc; ++c) {
+          const SumChunk sc = sum_chunk(t, c);
+          const int st = kc & 1;
+          ptx::mbar_wait(&sm.kv_empty[st], ((kc >> 1) & 1) ^ 1, status, 0x12000000u | st);
+          if (lane == 0) {
             ptx::mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kAtoms * kAtomBytes);
 #pragma unroll
             for (int a = 0; a < kAtoms; ++a) {
-              ptx::tma_load_3d(sm.k[st] + a * kAtomBytes, &tm_kbar, &sm.kv_full[st], a * 64, sc.w,
-                               t.bh);
-              ptx::tma_load_3d(sm.v[st] + a * kAtomBytes, &tm_vbar, &sm.kv_full[st], a * 64, sc.w,
-                               t.bh);
+              ptx::tma_load_3d(sm.k[st] + a * kAtomBytes, &tm_kbar, &sm.kv_full[st], a * 64,
+                               sc.w, t.bh);
+              ptx::tma_load_3d(sm.v[st] + a * kAtomBytes, &tm_vbar, &sm.kv_full[st], a * 64,
+                               sc.w, t.bh);
             }
-            ++kc;
           }
+          ++kc;
         }
-        ++tc;
       }
+      ++tc;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -419,9 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ptid == 0) {
           ptx::mbar_arrive(&sm.kv_empty[st]);
           __threadfence();
-          uint32_t* fl = p.flags + (size_t)t.bh * p.flags_stride;
-          if (t.s > 0) ptx::flag_wait(fl + t.s - 1, token, status, (uint32_t)n);
-          ptx::st_release_gpu(fl + t.s, token);
+          ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
         }
         ++kc;
       }

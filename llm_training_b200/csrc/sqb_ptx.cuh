@@ -132,6 +132,43 @@ __device__ __forceinline__ bool flag_wait(const uint32_t* flag, uint32_t want, u
   }
 }
 
+// Warp-collective: spins until flags[lo..hi) all equal `want` (each lane polls
+// every 32nd flag), then __syncwarp so every lane is ordered after all the
+// acquires.  Bounded like mbar_wait; returns false if it gave up.
+__device__ __forceinline__ bool flags_wait_range(const uint32_t* flags, int lo, int hi,
+                                                 uint32_t want, uint32_t* status,
+                                                 uint32_t detail) {
+  const int lane = threadIdx.x & 31;
+  uint64_t t0 = 0;
+  bool timed = false;
+  bool done = false;
+  while (true) {
+    bool ok = true;
+    for (int i = lo + lane; i < hi; i += 32) ok &= (ld_acquire_gpu(flags + i) == want);
+    if (__all_sync(0xffffffffu, ok)) {
+      done = true;
+      break;
+    }
+    int stop = 0;  // decided by lane 0 so the warp leaves the loop together
+    if (lane == 0) {
+      if (!timed) {
+        t0 = globaltimer();
+        timed = true;
+      }
+      if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {
+        stop = 1;
+      } else if (globaltimer() - t0 > kWaitBudgetNs) {
+        record_status(status, SQB_ERR_TIMEOUT, detail);
+        stop = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, stop, 0)) break;
+    __nanosleep(40);
+  }
+  __syncwarp();
+  return done;
+}
+
 // Generic-proxy global writes <-> async-proxy (TMA) accesses of this thread.
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");

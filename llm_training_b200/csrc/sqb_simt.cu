@@ -330,7 +330,12 @@ int backward_t(const Problem& p, TensorView q, TensorView k, TensorView v, Tenso
                                    dq);
   if (int e = launch_status()) return e;
   dkdv_kernel<E><<<rows, nt, 0, s>>>(p, q, k, v, dout, lse, delta, dkbar, dvbar, dk, dv);
-  return launch_status();
+  if (int e = launch_status()) return e;
+  // leave the summary-gradient scratch zeroed: the tcgen05 backward
+  // accumulates into the same workspace region and expects zeros
+  if (p.Gc > 0 && cudaMemsetAsync(ws + wl.dkbar, 0, wl.total - wl.dkbar, s) != cudaSuccess)
+    return SQB_ERR_CUDA;
+  return SQB_OK;
 }
 
 }  // namespace

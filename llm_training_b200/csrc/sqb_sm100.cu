@@ -92,9 +92,9 @@ bool sm100_fwd_supported(const Problem& p, std::initializer_list<TensorView> vie
   return common_ok(p, views, lse, kbar, vbar);
 }
 
-bool sm100_bwd_supported(const Problem&, std::initializer_list<TensorView>, const float*,
-                         const void*, const void*) {
-  return false;
+bool sm100_bwd_supported(const Problem& p, std::initializer_list<TensorView> views,
+                         const float* lse, const void* kbar, const void* vbar) {
+  return common_ok(p, views, lse, kbar, vbar);
 }
 
 int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,
@@ -117,10 +117,27 @@ int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, Te
   return sm100::launch_forward(p, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
 }
 
-int sm100_backward(const Problem&, TensorView, TensorView, TensorView, TensorView, TensorView,
-                   const float*, const void*, const void*, TensorView, TensorView, TensorView,
-                   uint8_t*, const WorkspaceLayout&, cudaStream_t) {
-  return SQB_ERR_UNSUPPORTED;
+int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,
+                   TensorView dout, const float* lse, const void* kbar, const void* vbar,
+                   TensorView dq, TensorView dk, TensorView dv, uint8_t* ws,
+                   const WorkspaceLayout& wl, cudaStream_t stream) {
+  int num_sms = 0;
+  if (!device_ok(&num_sms)) return SQB_ERR_DEVICE;
+  const int R = sm100::tile_rows(p.b);
+  sm100::BwdTensorMaps tm;
+  if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) ||
+      !encode_bthd(&tm.v, p, v, R) || !encode_bthd(&tm.dout, p, dout, R) ||
+      !encode_bthd(&tm.dq, p, dq, R) || !encode_bthd(&tm.dk, p, dk, R) ||
+      !encode_bthd(&tm.dv, p, dv, R))
+    return SQB_ERR_CUDA;
+  if (p.Gc > 0) {
+    if (!encode_summaries(&tm.kbar, p, kbar) || !encode_summaries(&tm.vbar, p, vbar))
+      return SQB_ERR_CUDA;
+  } else {
+    tm.kbar = tm.k;  // never read: no summaries
+    tm.vbar = tm.v;
+  }
+  return sm100::launch_backward(p, tm, lse, o, ws, wl, num_sms, stream);
 }
 
 }  // namespace sqb

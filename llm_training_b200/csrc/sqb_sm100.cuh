@@ -39,5 +39,12 @@ struct TensorMaps {
 int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
                    uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream);
 
+struct BwdTensorMaps {
+  CUtensorMap q, k, v, dout, dq, dk, dv, kbar, vbar;
+};
+
+int launch_backward(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
+                    uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream);
+
 }  // namespace sm100
 }  // namespace sqb

@@ -22,7 +22,7 @@ __all__ = ["sqrt_block_attention", "sqrt_block_forward", "sqrt_block_backward", 
 _DTYPES = {torch.float32: _lib.SQB_F32, torch.bfloat16: _lib.SQB_BF16}
 
 _ws_lock = threading.Lock()
-_workspaces: dict[int, torch.Tensor] = {}
+_workspaces: dict[tuple, torch.Tensor] = {}
 
 
 def block_geometry(T: int, block: int | None = None):
@@ -30,19 +30,22 @@ def block_geometry(T: int, block: int | None = None):
     return _lib.geometry(T, block)
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-device zero-initialised scratch, grown on demand.
+def _workspace(device: torch.device, shape: tuple) -> torch.Tensor:
+    """Zero-initialised scratch for one (B, T, H, D, b) problem on one device.
 
     The kernels keep it clean between calls (flags are epoch-stamped and the
-    summary-gradient accumulators are re-zeroed by their consumer), so it is
-    zeroed only when allocated.  Calls on one device must share one stream.
+    summary-gradient accumulators end every call at zero), so it is zeroed
+    only when allocated.  The region layout depends on the problem shape,
+    hence one workspace per shape.  Calls on one device must share one stream.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx,) + tuple(int(x) for x in shape)
     with _ws_lock:
-        ws = _workspaces.get(idx)
-        if ws is None or ws.numel() < nbytes:
-            ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
-            _workspaces[idx] = ws
+        ws = _workspaces.get(key)
+        if ws is None:
+            nbytes = _lib.workspace_bytes(*shape)
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
         return ws
 
 
@@ -91,8 +94,7 @@ def sqrt_block_forward(q, k, v, block=None, scale=None, impl="auto"):
     lse = torch.empty((B, H, T), dtype=torch.float32, device=dev)
     kbar = torch.empty((B, H, Gc, D), dtype=q.dtype, device=dev)
     vbar = torch.empty((B, H, Gc, D), dtype=q.dtype, device=dev)
-    nbytes = _lib.workspace_bytes(B, T, H, D, b)
-    ws = _workspace(dev, nbytes)
+    ws = _workspace(dev, (B, T, H, D, b))
     stream = torch.cuda.current_stream(dev).cuda_stream
     st = _lib.strides_array(_strides(q), _strides(k), _strides(v), _strides(o))
     rc = _lib.lib().sqb_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
@@ -119,8 +121,7 @@ def sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block=None, scale=Non
     dq = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
     dk = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
     dv = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
-    nbytes = _lib.workspace_bytes(B, T, H, D, b)
-    ws = _workspace(dev, nbytes)
+    ws = _workspace(dev, (B, T, H, D, b))
     stream = torch.cuda.current_stream(dev).cuda_stream
     st = _lib.strides_array(*(_strides(t) for t in (q, k, v, o, dout, dq, dk, dv)))
     lse = lse.contiguous()
@@ -135,16 +136,22 @@ def sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block=None, scale=Non
 
 
 def read_status(device=None) -> int:
-    """Synchronize and return (then clear) the device-side status of the workspace."""
-    dev = torch.device("cuda", device if isinstance(device, int) else
-                       (device.index if device is not None and device.index is not None
-                        else torch.cuda.current_device()))
-    ws = _workspaces.get(dev.index)
-    if ws is None:
-        return _lib.SQB_OK
-    detail = _lib.ctypes.c_int64()
-    return _lib.lib().sqb_read_status(ws.data_ptr(), torch.cuda.current_stream(dev).cuda_stream,
-                                      _lib.ctypes.byref(detail))
+    """Synchronize and return (then clear) the first device-side status
+    recorded in any workspace of the device (0 = ok)."""
+    idx = device if isinstance(device, int) else (
+        device.index if device is not None and device.index is not None
+        else torch.cuda.current_device())
+    dev = torch.device("cuda", idx)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    status = _lib.SQB_OK
+    for key, ws in list(_workspaces.items()):
+        if key[0] != idx:
+            continue
+        detail = _lib.ctypes.c_int64()
+        rc = _lib.lib().sqb_read_status(ws.data_ptr(), stream, _lib.ctypes.byref(detail))
+        if rc != _lib.SQB_OK and status == _lib.SQB_OK:
+            status = rc
+    return status
 
 
 class _SqrtBlockAttention(torch.autograd.Function):

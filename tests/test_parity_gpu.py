@@ -138,12 +138,24 @@ def test_strided_projection_views(dtype):
     check(q, k, v, do, None, got, dtype)
 
 
-def test_repeatable_bitwise():
+@pytest.mark.parametrize("impl", ["simt", "tcgen05"])
+def test_repeatable(impl):
+    """O, LSE and dQ are bit-identical run to run.  dK/dV are too on the SIMT
+    path; the tcgen05 backward adds each block's summary gradient from many
+    CTAs with fp32 atomics, so the order of those additions - and at most the
+    last bf16 bit of dK/dV - can change between runs."""
     q, k, v, do = inputs(1, 4, 2048, 128, 5, torch.bfloat16)
-    a = run(q, k, v, do, None, "auto")
-    c = run(q, k, v, do, None, "auto")
-    for x, y in zip(a, c):
-        assert torch.equal(x, y)
+    a = run(q, k, v, do, None, impl)
+    c = run(q, k, v, do, None, impl)
+    for name, x, y in zip(("o", "lse", "dq"), a[:3], c[:3]):
+        assert torch.equal(x, y), name
+    for name, x, y in zip(("dk", "dv"), a[3:], c[3:]):
+        if impl == "simt":
+            assert torch.equal(x, y), name
+        else:
+            d = (x.float() - y.float()).abs()
+            assert (d <= 2.0 ** -7 * x.float().abs().clamp_min(1e-3)).all(), name
+            assert (d > 0).float().mean().item() < 0.01, name
 
 
 @pytest.mark.parametrize("T", [4096, 16384, 65536])
