@@ -250,7 +250,7 @@ def run_ours(args, world, rank, local):
     with ClockSampler(torch.cuda.current_device()) as clocks:
         # warm up for at least W steps and ~0.5 s so the clock sampler (100 ms
         # period) has samples under load when the timed region starts
-        t_end = time.perf_counter() + 0.5
+        t_end = time.perf_counter() + args.warmup_seconds
         i = 0
         while i < max(args.warmup, 3) or time.perf_counter() < t_end:
             step()
@@ -316,7 +316,7 @@ def run_ours(args, world, rank, local):
                         "GBps": round(fwd_bytes / (fwd_ms * 1e-3) / 1e9, 1)},
                 "bwd": {"ms": round(bwd_ms, 4),
                         "GBps": round(bwd_bytes / (bwd_ms * 1e-3) / 1e9, 1)}}
-    traffic_path = os.path.join(REPO, "profiles", "traffic.json")
+    traffic_path = os.path.join(REPO, "profiles", "dram_traffic.json")
     if os.path.exists(traffic_path):
         try:
             roofline["traffic"] = json.load(open(traffic_path)).get(dom[0])
@@ -362,6 +362,8 @@ def main():
     ap.add_argument("--kernels", choices=["auto", "tcgen05", "simt"], default="auto")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--warmup-seconds", type=float, default=0.5,
+                    help="keep warming up at least this long (clock sampler needs samples)")
     args = ap.parse_args()
     world, rank, local = init_dist()
     try:
