@@ -103,6 +103,22 @@ int sqb_bwd(const void* q, const void* k, const void* v, const void* o,
             int64_t block, const int64_t* strides, int dtype, float scale, int impl,
             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Backward without a caller-supplied workspace.  This entry point has no
+ * counterpart in the reference.  It is for callers that cannot allocate device
+ * memory where they run the backward (their memory is owned by another
+ * component, or their footprint is fixed after start-up): the scratch lives in
+ * one 8 MiB array the library holds on every GPU it is loaded on.  Arguments
+ * are those of sqb_bwd without the workspace.  Problems whose
+ * sqb_workspace_bytes exceeds 8 MiB return SQB_ERR_WORKSPACE.  The first call on
+ * a device looks up the array's address; make it before any stream capture.
+ * Each call clears the scratch it uses; all calls on a device share it, so calls
+ * that overlap on the GPU race and must not be issued.  Allocates nothing. */
+int sqb_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                    const void* dout, const float* lse, const void* kbar, const void* vbar,
+                    void* dq, void* dk, void* dv, int64_t B, int64_t T, int64_t H, int64_t D,
+                    int64_t block, const int64_t* strides, int dtype, float scale, int impl,
+                    void* stream);
+
 /* Synchronizes `stream`, returns the device-side status recorded in the
  * workspace (SQB_OK or SQB_ERR_TIMEOUT) and clears it.  `detail`, if not
  * NULL, receives the index of the work tile that reported the failure. */
