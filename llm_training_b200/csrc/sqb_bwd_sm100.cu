@@ -55,8 +55,9 @@ struct BwdSmem {
   alignas(1024) uint8_t dout[kTileBytes];  // dO
   alignas(1024) uint8_t k[kTileBytes];     // K chunk, then dK staging
   alignas(1024) uint8_t v[kTileBytes];     // V chunk, then dV staging
-  alignas(1024) uint8_t p[2 * kAtomBytes];   // P  (128 query rows x 128 key cols)
+  alignas(1024) uint8_t p[2 * kAtomBytes];   // O (for delta), then P (128 x 128 keys)
   alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout)
+  float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
   uint64_t ld_full, q_empty, kv_full, kv_empty, s_full, ps_full, g_full, g_free;
   int tile_ring;
   uint32_t tmem_base;
@@ -75,7 +76,8 @@ __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w &
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+               const __grid_constant__ CUtensorMap tm_do,
                const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
                const __grid_constant__ CUtensorMap tm_dv,
                const __grid_constant__ CUtensorMap tm_kbar,
@@ -135,12 +137,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const Tile t = tile_of(n);
-        ptx::mbar_arrive_expect_tx(&sm.ld_full, 2 * kAtoms * box_bytes);
+        ptx::mbar_arrive_expect_tx(&sm.ld_full, 3 * kAtoms * box_bytes);
 #pragma unroll
         for (int a = 0; a < kAtoms; ++a) {
           ptx::tma_load_4d(sm.q + a * kAtomBytes, &tm_q, &sm.ld_full, a * 64, t.h, t.r0, t.n);
           ptx::tma_load_4d(sm.dout + a * kAtomBytes, &tm_do, &sm.ld_full, a * 64, t.h, t.r0,
                            t.n);
+          ptx::tma_load_4d(sm.p + a * kAtomBytes, &tm_o, &sm.ld_full, a * 64, t.h, t.r0, t.n);
         }
         for (int c = 0; c <= t.nsc; ++c) {
           ptx::mbar_wait(&sm.kv_empty, (kc & 1) ^ 1, status, 0x51000000u);
@@ -230,14 +233,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int blk_t = valid ? tq / p.g.b : 0;
       const int lim = valid ? min(blk_t, p.g.Gc) : 0;
       const float L = valid ? p.lse[(size_t)t.bh * p.g.T + tq] * kLog2e : 0.f;
-      float delta = 0.f;
+      float delta = 0.f;  // O was loaded into the P buffer; this row only
       if (valid) {
-        const uint4* orow = reinterpret_cast<const uint4*>(
-            p.o + t.n * p.o_sb + (int64_t)tq * p.o_st + t.h * p.o_sh);
 #pragma unroll 4
         for (int cc = 0; cc < D / 8; ++cc) {
-          const uint4 a = orow[cc];
-          const uint4 g = *reinterpret_cast<const uint4*>(sm.dout + swz_offset(row, cc * 8));
+          const uint32_t off = swz_offset(row, cc * 8);
+          const uint4 a = *reinterpret_cast<const uint4*>(sm.p + off);
+          const uint4 g = *reinterpret_cast<const uint4*>(sm.dout + off);
           delta += bf16lo(a.x) * bf16lo(g.x) + bf16hi(a.x) * bf16hi(g.x) +
                    bf16lo(a.y) * bf16lo(g.y) + bf16hi(a.y) * bf16hi(g.y) +
                    bf16lo(a.z) * bf16lo(g.z) + bf16hi(a.z) * bf16hi(g.z) +
@@ -257,6 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, s);
             ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, dp);
             ptx::tmem_wait_ld();
+            ptx::reg_fence(s);
+            ptx::reg_fence(dp);
           }
 #pragma unroll
           for (int j8 = 0; j8 < 4; ++j8) {
@@ -304,17 +308,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, gv);
           ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, gk);
           ptx::tmem_wait_ld();
+          ptx::reg_fence(gv);
+          ptx::reg_fence(gk);
           if (ok) {
 #pragma unroll
             for (int j4 = 0; j4 < 8; ++j4) {
-              atomicAdd(reinterpret_cast<float4*>(dvrow + pc * 32 + 4 * j4),
-                        make_float4(__uint_as_float(gv[4 * j4]), __uint_as_float(gv[4 * j4 + 1]),
-                                    __uint_as_float(gv[4 * j4 + 2]),
-                                    __uint_as_float(gv[4 * j4 + 3])));
-              atomicAdd(reinterpret_cast<float4*>(dkrow + pc * 32 + 4 * j4),
-                        make_float4(__uint_as_float(gk[4 * j4]), __uint_as_float(gk[4 * j4 + 1]),
-                                    __uint_as_float(gk[4 * j4 + 2]),
-                                    __uint_as_float(gk[4 * j4 + 3])));
+              ptx::red_add_v4(dvrow + pc * 32 + 4 * j4, __uint_as_float(gv[4 * j4]),
+                              __uint_as_float(gv[4 * j4 + 1]), __uint_as_float(gv[4 * j4 + 2]),
+                              __uint_as_float(gv[4 * j4 + 3]));
+              ptx::red_add_v4(dkrow + pc * 32 + 4 * j4, __uint_as_float(gk[4 * j4]),
+                              __uint_as_float(gk[4 * j4 + 1]), __uint_as_float(gk[4 * j4 + 2]),
+                              __uint_as_float(gk[4 * j4 + 3]));
             }
           }
         }
@@ -325,29 +329,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kc;
       }
 
-      // ---- this tile's additions are done: publish
+      // ---- in-block chunk
+      softmax_grad(t.n_in, valid ? blk_t * p.g.b - t.r0 : 0, valid ? row + 1 : 0);
+      // ---- publish this tile's summary-gradient additions.  Done only now,
+      // after the in-block MMAs, so the fence finds the reductions issued
+      // during the summary chunks long completed instead of waiting for them.
       __threadfence();
       ptx::named_barrier(1, 128);
       if (stid == 0)
         ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
-
-      // ---- in-block chunk, then the epilogue
-      softmax_grad(t.n_in, valid ? blk_t * p.g.b - t.r0 : 0, valid ? row + 1 : 0);
       // every later tile of this sequence has added to the summary sums
       if (stid < 32)
         ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT, token,
                               status, (uint32_t)n);
       ptx::named_barrier(1, 128);
+      // the summary gradient is block-uniform: stage sum / b of each of the
+      // tile's complete blocks in smem once, and re-zero the consumed sums
+      const int nfull = max(0, min(p.g.R / p.g.b, p.g.Gc - t.blk0));
+      for (int lb = 0; lb < nfull; ++lb) {
+        const size_t base = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D;
+        for (int i = stid; i < D; i += 128) {
+          sm.sgrad[0][lb][i] = __ldcg(p.dkbar + base + i) * inv_b;
+          sm.sgrad[1][lb][i] = __ldcg(p.dvbar + base + i) * inv_b;
+          p.dkbar[base + i] = 0.f;
+          p.dvbar[base + i] = 0.f;
+        }
+      }
+      ptx::named_barrier(1, 128);
       {
         const bool complete = valid && blk_t < p.g.Gc;  // this lane's key is in a full block
-        const float* skrow = p.dkbar + ((size_t)t.bh * p.g.Gc + blk_t) * D;
-        const float* svrow = p.dvbar + ((size_t)t.bh * p.g.Gc + blk_t) * D;
+        const int lb_t = valid ? blk_t - t.blk0 : 0;
+        const float* skrow = sm.sgrad[0][lb_t];
+        const float* svrow = sm.sgrad[1][lb_t];
 #pragma unroll 1
         for (int pc = 0; pc < D / 32; ++pc) {
           uint32_t gv[32], gk[32];
           ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, gv);
           ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, gk);
           ptx::tmem_wait_ld();
+          ptx::reg_fence(gv);
+          ptx::reg_fence(gk);
 #pragma unroll
           for (int j8 = 0; j8 < 4; ++j8) {
             float fk[8], fv[8];
@@ -358,16 +379,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (complete) {
               const int col = pc * 32 + j8 * 8;
-              const float4 k0 = __ldcg(reinterpret_cast<const float4*>(skrow + col));
-              const float4 k1 = __ldcg(reinterpret_cast<const float4*>(skrow + col + 4));
-              const float4 v0 = __ldcg(reinterpret_cast<const float4*>(svrow + col));
-              const float4 v1 = __ldcg(reinterpret_cast<const float4*>(svrow + col + 4));
-              fk[0] += k0.x * inv_b; fk[1] += k0.y * inv_b; fk[2] += k0.z * inv_b;
-              fk[3] += k0.w * inv_b; fk[4] += k1.x * inv_b; fk[5] += k1.y * inv_b;
-              fk[6] += k1.z * inv_b; fk[7] += k1.w * inv_b;
-              fv[0] += v0.x * inv_b; fv[1] += v0.y * inv_b; fv[2] += v0.z * inv_b;
-              fv[3] += v0.w * inv_b; fv[4] += v1.x * inv_b; fv[5] += v1.y * inv_b;
-              fv[6] += v1.z * inv_b; fv[7] += v1.w * inv_b;
+              const float4 k0 = *reinterpret_cast<const float4*>(skrow + col);
+              const float4 k1 = *reinterpret_cast<const float4*>(skrow + col + 4);
+              const float4 v0 = *reinterpret_cast<const float4*>(svrow + col);
+              const float4 v1 = *reinterpret_cast<const float4*>(svrow + col + 4);
+              fk[0] += k0.x; fk[1] += k0.y; fk[2] += k0.z; fk[3] += k0.w;
+              fk[4] += k1.x; fk[5] += k1.y; fk[6] += k1.z; fk[7] += k1.w;
+              fv[0] += v0.x; fv[1] += v0.y; fv[2] += v0.z; fv[3] += v0.w;
+              fv[4] += v1.x; fv[5] += v1.y; fv[6] += v1.z; fv[7] += v1.w;
             }
             const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
             *reinterpret_cast<uint4*>(sm.k + off) =
@@ -386,6 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t gq[32];
           ptx::tmem_ld32(tmem + lane_off + kColDQ + pc * 32, gq);
           ptx::tmem_wait_ld();
+          ptx::reg_fence(gq);
 #pragma unroll
           for (int j8 = 0; j8 < 4; ++j8) {
             const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
@@ -399,16 +419,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::fence_proxy_async_smem();
         ptx::named_barrier(1, 128);
-        // re-zero the summary sums this tile consumed (all later adders are done)
-        const int nb = p.g.R / p.g.b;
-        const int nfull = max(0, min(nb, p.g.Gc - t.blk0));
-        for (int lb = 0; lb < nfull; ++lb) {
-          const size_t base = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D;
-          for (int i = stid; i < D; i += 128) {
-            p.dkbar[base + i] = 0.f;
-            p.dvbar[base + i] = 0.f;
-          }
-        }
         if (stid == 0) {
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a) {
@@ -475,8 +485,8 @@ int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorV
                            (int)smem) != cudaSuccess)
     return SQB_ERR_LAUNCH;
   const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
-  bwd_kernel<D><<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.dout, tm.dq, tm.dk, tm.dv,
-                                                   tm.kbar, tm.vbar, p);
+  bwd_kernel<D><<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.dout, tm.dq, tm.dk,
+                                                   tm.dv, tm.kbar, tm.vbar, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 

@@ -46,22 +46,37 @@ struct FwdParams {
   int flags_stride;
 };
 
-template <int D>
+// Pipeline depths: NQ query-tile slots, NKV key/value chunk stages, NS score
+// buffers in TMEM.  Depth 2 everywhere fills one SM with one CTA; depth 1
+// everywhere halves shared memory and TMEM so two CTAs share an SM and hide
+// each other's latencies.
+template <int D, int NQ, int NKV, int NS>
 struct FwdSmem {
   static constexpr int kTileBytes = (D / 64) * kAtomBytes;
-  alignas(1024) uint8_t q[2][kTileBytes];
-  alignas(1024) uint8_t k[2][kTileBytes];
-  alignas(1024) uint8_t v[2][kTileBytes];
+  alignas(1024) uint8_t q[NQ][kTileBytes];
+  alignas(1024) uint8_t k[NKV][kTileBytes];
+  alignas(1024) uint8_t v[NKV][kTileBytes];
   float red[4][2][D];
-  uint64_t q_full[2], q_empty[2], kv_full[2], kv_empty[2];
-  uint64_t s_full[2], p_full[2], s_free[2], o_full, o_free;
-  int tile_ring[2];
+  uint64_t q_full[NQ], q_empty[NQ];
+  uint64_t k_full[NKV], k_empty[NKV], v_full[NKV], v_empty[NKV];
+  uint64_t s_full[NS], p_full[NS], s_free[NS], o_full, o_free;
+  int tile_ring[NQ];
   uint32_t tmem_base;
 };
 
 constexpr int kThreads = 320;
-constexpr uint32_t kTmemCols = 512;
 constexpr float kLn2 = 0.6931471805599453f;
+
+// TMEM columns: NS score buffers of 128 columns, then O (D columns); the
+// allocation is a power of two >= 32.
+__host__ __device__ constexpr uint32_t fwd_tmem_cols(int D, int NS) {
+  return (NS * 128 + D) <= 256 ? 256u : 512u;
+}
+
+template <int NQ, int NKV, int NS>
+constexpr int ctas_per_sm() {
+  return (NQ == 1 && NKV == 1 && NS == 1) ? 2 : 1;
+}
 
 __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 q) {
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
@@ -72,28 +87,35 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 q) {
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int NQ, int NKV, int NS>
+__global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                const __grid_constant__ CUtensorMap tm_kbar,
                const __grid_constant__ CUtensorMap tm_vbar, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
-  FwdSmem<D>& sm = *reinterpret_cast<FwdSmem<D>*>(
+  FwdSmem<D, NQ, NKV, NS>& sm = *reinterpret_cast<FwdSmem<D, NQ, NKV, NS>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   uint32_t* status = p.ctrl + kStatus;
   const uint32_t token = *reinterpret_cast<volatile uint32_t*>(p.ctrl + kFwdEpoch) + 1u;
   constexpr int kAtoms = D / 64;
+  constexpr uint32_t kTmemCols = fwd_tmem_cols(D, NS);
   const uint32_t box_bytes = (uint32_t)p.g.R * 128u;  // one atom of an R-row box
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NQ; ++i) {
       ptx::mbar_init(&sm.q_full[i], 1);
       ptx::mbar_init(&sm.q_empty[i], 2);   // epilogue store done + pooling done
-      ptx::mbar_init(&sm.kv_full[i], 1);
-      ptx::mbar_init(&sm.kv_empty[i], 2);  // PV mma complete + pooling done
+    }
+    for (int i = 0; i < NKV; ++i) {
+      ptx::mbar_init(&sm.k_full[i], 1);
+      ptx::mbar_init(&sm.k_empty[i], 2);  // S mma complete + pooling done
+      ptx::mbar_init(&sm.v_full[i], 1);
+      ptx::mbar_init(&sm.v_empty[i], 2);  // PV mma complete + pooling done
+    }
+    for (int i = 0; i < NS; ++i) {
       ptx::mbar_init(&sm.s_full[i], 1);
       ptx::mbar_init(&sm.p_full[i], 4);    // one arrive per softmax warp
       ptx::mbar_init(&sm.s_free[i], 1);
@@ -123,14 +145,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // lane 0 claims tiles and issues every TMA and barrier operation.
     int tc = 0, kc = 0;
     while (true) {
-      const int slot = tc & 1;
+      const int slot = tc % NQ;
       int n = 0;
       if (lane == 0) {
         n = (int)atomicAdd(p.ctrl + kFwdTileCounter, 1u);
         if (n >= p.total_tiles) n = -1;
       }
       n = __shfl_sync(0xffffffffu, n, 0);
-      ptx::mbar_wait(&sm.q_empty[slot], ((tc >> 1) & 1) ^ 1, status, 0x10000000u | slot);
+      ptx::mbar_wait(&sm.q_empty[slot], ((tc / NQ) & 1) ^ 1, status, 0x10000000u | slot);
       if (lane == 0) {
         sm.tile_ring[slot] = n;
         if (n < 0) ptx::mbar_arrive(&sm.q_full[slot]);
@@ -145,17 +167,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                            t.r0, t.n);
       }
       {
-        const int st = kc & 1;
-        ptx::mbar_wait(&sm.kv_empty[st], ((kc >> 1) & 1) ^ 1, status, 0x11000000u | st);
+        const int st = kc % NKV;
+        const uint32_t par = ((kc / NKV) & 1) ^ 1;
+        ptx::mbar_wait(&sm.k_empty[st], par, status, 0x11000000u | st);
         if (lane == 0) {
-          ptx::mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kAtoms * box_bytes);
+          ptx::mbar_arrive_expect_tx(&sm.k_full[st], kAtoms * box_bytes);
 #pragma unroll
-          for (int a = 0; a < kAtoms; ++a) {
-            ptx::tma_load_4d(sm.k[st] + a * kAtomBytes, &tm_k, &sm.kv_full[st], a * 64, t.h,
+          for (int a = 0; a < kAtoms; ++a)
+            ptx::tma_load_4d(sm.k[st] + a * kAtomBytes, &tm_k, &sm.k_full[st], a * 64, t.h,
                              t.r0, t.n);
-            ptx::tma_load_4d(sm.v[st] + a * kAtomBytes, &tm_v, &sm.kv_full[st], a * 64, t.h,
+        }
+        ptx::mbar_wait(&sm.v_empty[st], par, status, 0x13000000u | st);
+        if (lane == 0) {
+          ptx::mbar_arrive_expect_tx(&sm.v_full[st], kAtoms * box_bytes);
+#pragma unroll
+          for (int a = 0; a < kAtoms; ++a)
+            ptx::tma_load_4d(sm.v[st] + a * kAtomBytes, &tm_v, &sm.v_full[st], a * 64, t.h,
                              t.r0, t.n);
-          }
         }
         ++kc;
       }
@@ -167,17 +195,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) ptx::fence_proxy_async_global();
         for (int c = 0; c < t.nsc; ++c) {
           const SumChunk sc = sum_chunk(t, c);
-          const int st = kc & 1;
-          ptx::mbar_wait(&sm.kv_empty[st], ((kc >> 1) & 1) ^ 1, status, 0x12000000u | st);
+          const int st = kc % NKV;
+          const uint32_t par = ((kc / NKV) & 1) ^ 1;
+          ptx::mbar_wait(&sm.k_empty[st], par, status, 0x12000000u | st);
           if (lane == 0) {
-            ptx::mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kAtoms * kAtomBytes);
+            ptx::mbar_arrive_expect_tx(&sm.k_full[st], kAtoms * kAtomBytes);
 #pragma unroll
-            for (int a = 0; a < kAtoms; ++a) {
-              ptx::tma_load_3d(sm.k[st] + a * kAtomBytes, &tm_kbar, &sm.kv_full[st], a * 64,
+            for (int a = 0; a < kAtoms; ++a)
+              ptx::tma_load_3d(sm.k[st] + a * kAtomBytes, &tm_kbar, &sm.k_full[st], a * 64,
                                sc.w, t.bh);
-              ptx::tma_load_3d(sm.v[st] + a * kAtomBytes, &tm_vbar, &sm.kv_full[st], a * 64,
+          }
+          ptx::mbar_wait(&sm.v_empty[st], par, status, 0x14000000u | st);
+          if (lane == 0) {
+            ptx::mbar_arrive_expect_tx(&sm.v_full[st], kAtoms * kAtomBytes);
+#pragma unroll
+            for (int a = 0; a < kAtoms; ++a)
+              ptx::tma_load_3d(sm.v[st] + a * kAtomBytes, &tm_vbar, &sm.v_full[st], a * 64,
                                sc.w, t.bh);
-            }
           }
           ++kc;
         }
@@ -187,13 +221,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t s_tmem[2] = {tmem, tmem + 128};
-      const uint32_t o_tmem = tmem + 256;
+      const uint32_t o_tmem = tmem + NS * 128;
       const uint32_t idesc_pv = ptx::idesc_bf16(128, D, false, true);
       int tc = 0, kc = 0, gc = 0;
       while (true) {
-        const int slot = tc & 1;
-        ptx::mbar_wait(&sm.q_full[slot], (tc >> 1) & 1, status, 0x20000000u | slot);
+        const int slot = tc % NQ;
+        ptx::mbar_wait(&sm.q_full[slot], (tc / NQ) & 1, status, 0x20000000u | slot);
         const int n = sm.tile_ring[slot];
         if (n < 0) break;
         const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
@@ -201,32 +234,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t q_saddr = ptx::smem_u32(sm.q[slot]);
         auto chunk_n = [&](int c) { return c == 0 ? t.n_in : sum_chunk(t, c - 1).n16; };
         auto issue_pv = [&](int c) {
-          const int g = gc + c, x = g & 1, st = (kc + c) & 1;
-          ptx::mbar_wait(&sm.p_full[x], (g >> 1) & 1, status, 0x21000000u | x);
+          const int g = gc + c, x = g % NS, st = (kc + c) % NKV;
+          ptx::mbar_wait(&sm.p_full[x], (g / NS) & 1, status, 0x21000000u | x);
+          ptx::mbar_wait(&sm.v_full[st], ((kc + c) / NKV) & 1, status, 0x25000000u | st);
           if (c == 0 && tc > 0) ptx::mbar_wait(&sm.o_free, (tc - 1) & 1, status, 0x22000000u);
           ptx::tc_fence_after();
           const uint32_t v_saddr = ptx::smem_u32(sm.v[st]);
           const int nk = chunk_n(c) / 16;
           for (int kk = 0; kk < nk; ++kk)
-            ptx::mma_ts(o_tmem, s_tmem[x] + kk * 8, desc_mnmajor(v_saddr, kk), idesc_pv,
+            ptx::mma_ts(o_tmem, tmem + x * 128 + kk * 8, desc_mnmajor(v_saddr, kk), idesc_pv,
                         (c > 0 || kk > 0) ? 1u : 0u);
-          ptx::mma_commit(&sm.kv_empty[st]);
+          ptx::mma_commit(&sm.v_empty[st]);
           ptx::mma_commit(&sm.s_free[x]);
           if (c == nch - 1) ptx::mma_commit(&sm.o_full);
         };
+        // With two score buffers and two K/V stages, S(c) is issued before
+        // PV(c-1) so the QK^T of the next chunk overlaps the softmax of this
+        // one; with single buffers S(c) needs both freed by PV(c-1), which
+        // therefore goes first.
+        constexpr bool kOverlap = NS >= 2 && NKV >= 2;
         for (int c = 0; c < nch; ++c) {
-          const int g = gc + c, x = g & 1, st = (kc + c) & 1;
-          ptx::mbar_wait(&sm.kv_full[st], ((kc + c) >> 1) & 1, status, 0x23000000u | st);
-          if (g >= 2) ptx::mbar_wait(&sm.s_free[x], ((g - 2) >> 1) & 1, status, 0x24000000u | x);
+          if (!kOverlap && c >= 1) issue_pv(c - 1);
+          const int g = gc + c, x = g % NS, st = (kc + c) % NKV;
+          ptx::mbar_wait(&sm.k_full[st], ((kc + c) / NKV) & 1, status, 0x23000000u | st);
+          if (g >= NS)
+            ptx::mbar_wait(&sm.s_free[x], ((g - NS) / NS) & 1, status, 0x24000000u | x);
           ptx::tc_fence_after();
           const uint32_t k_saddr = ptx::smem_u32(sm.k[st]);
           const uint32_t idesc_s = ptx::idesc_bf16(128, chunk_n(c), false, false);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            ptx::mma_ss(s_tmem[x], desc_kmajor(q_saddr, kk), desc_kmajor(k_saddr, kk), idesc_s,
+            ptx::mma_ss(tmem + x * 128, desc_kmajor(q_saddr, kk), desc_kmajor(k_saddr, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
           ptx::mma_commit(&sm.s_full[x]);
-          if (c >= 1) issue_pv(c - 1);
+          ptx::mma_commit(&sm.k_empty[st]);
+          if (kOverlap && c >= 1) issue_pv(c - 1);
         }
         issue_pv(nch - 1);
         gc += nch;
@@ -239,11 +281,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t o_addr = tmem + lane_off + 256;
+    const uint32_t o_addr = tmem + lane_off + NS * 128;
     int tc = 0, gc = 0;
     while (true) {
-      const int slot = tc & 1;
-      ptx::mbar_wait(&sm.q_full[slot], (tc >> 1) & 1, status, 0x30000000u | slot);
+      const int slot = tc % NQ;
+      ptx::mbar_wait(&sm.q_full[slot], (tc / NQ) & 1, status, 0x30000000u | slot);
       const int n = sm.tile_ring[slot];
       if (n < 0) break;
       const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
@@ -254,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int lim = valid ? min(blk_t, p.g.Gc) : 0;  // visible summaries j < lim
       float m = -INFINITY, l = 0.f;
       for (int c = 0; c < nch; ++c) {
-        const int g = gc + c, x = g & 1;
+        const int g = gc + c, x = g % NS;
         int N, vlo, vhi;  // MMA width and the valid column range [vlo, vhi)
         if (c == 0) {
           N = t.n_in;
@@ -266,19 +308,48 @@ __global__ void __launch_bounds__(kThreads, 1)
           vlo = sc.lo - sc.w;
           vhi = min(sc.e, lim) - sc.w;
         }
-        ptx::mbar_wait(&sm.s_full[x], (g >> 1) & 1, status, 0x31000000u | x);
+        ptx::mbar_wait(&sm.s_full[x], (g / NS) & 1, status, 0x31000000u | x);
         ptx::tc_fence_after();
         const uint32_t s_addr = tmem + lane_off + x * 128;
-        const int npieces = (N + 31) >> 5;
+        // 16-column pieces no row of this warp can see are skipped (in the
+        // causal in-block chunk with b = R = 128, warp q needs columns < 32q+32)
+        const bool any_col = vhi > vlo;
+        const int wlo = __reduce_min_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
+        const int whi = __reduce_max_sync(0xffffffffu, any_col ? vhi : 0);
+        const int nq = N >> 4;
+        const int q_lo = whi > wlo ? (wlo >> 4) : 0;
+        const int q_hi = whi > wlo ? min((whi + 15) >> 4, nq) : 0;
+        const uint32_t vspan = any_col ? (uint32_t)(vhi - vlo) : 0u;
+        // Both passes walk the live pieces with two 16-column buffers, issuing
+        // the next piece's TMEM load before this piece's math.
+        uint32_t bufA[16], bufB[16];
+        // pass 1: row max over the visible columns (masked -> -inf)
         float mx = -INFINITY;
-        for (int pc = 0; pc < npieces; ++pc) {
-          uint32_t r[32];
-          ptx::tmem_ld32(s_addr + pc * 32, r);
-          ptx::tmem_wait_ld();
+        {
+          auto maxp = [&](const uint32_t (&r)[16], int q) {
+            float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = pc * 32 + j;
-            if (col >= vlo && col < vhi) mx = fmaxf(mx, __uint_as_float(r[j]));
+            for (int j = 0; j < 16; j += 2) {
+              m0 = fmaxf(m0, (uint32_t)(q * 16 + j - vlo) < vspan ? __uint_as_float(r[j])
+                                                                  : -INFINITY);
+              m1 = fmaxf(m1, (uint32_t)(q * 16 + j + 1 - vlo) < vspan ? __uint_as_float(r[j + 1])
+                                                                      : -INFINITY);
+            }
+            mx = fmaxf(mx, fmaxf(m0, m1));
+          };
+          if (q_lo < q_hi) ptx::tmem_ld16(s_addr + q_lo * 16, bufA);
+          for (int q = q_lo; q < q_hi; q += 2) {
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(bufA);
+            const bool b = q + 1 < q_hi;
+            if (b) ptx::tmem_ld16(s_addr + q * 16 + 16, bufB);
+            maxp(bufA, q);
+            if (b) {
+              ptx::tmem_wait_ld();
+              ptx::reg_fence(bufB);
+              if (q + 2 < q_hi) ptx::tmem_ld16(s_addr + q * 16 + 32, bufA);
+              maxp(bufB, q + 1);
+            }
           }
         }
         const float m_new = fmaxf(m, mx * p.scale_log2);
@@ -286,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool need = m_new > m;
           if (__any_sync(0xffffffffu, need)) {
             // PV of the previous chunk must have landed before O is rescaled
-            ptx::mbar_wait(&sm.s_free[(g - 1) & 1], ((g - 1) >> 1) & 1, status, 0x32000000u);
+            ptx::mbar_wait(&sm.s_free[(g - 1) % NS], ((g - 1) / NS) & 1, status, 0x32000000u);
             ptx::tc_fence_after();
             const float alpha = need ? (m == -INFINITY ? 0.f : ptx::ex2(m - m_new)) : 1.f;
 #pragma unroll 1
@@ -294,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t r[32];
               ptx::tmem_ld32(o_addr + pc * 32, r);
               ptx::tmem_wait_ld();
+              ptx::reg_fence(r);
 #pragma unroll
               for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
               ptx::tmem_st32(o_addr + pc * 32, r);
@@ -304,24 +376,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         m = m_new;
         const float mm = (m == -INFINITY) ? 0.f : m;
-        for (int pc = 0; pc < npieces; ++pc) {
-          uint32_t r[32];
-          ptx::tmem_ld32(s_addr + pc * 32, r);
-          ptx::tmem_wait_ld();
-          uint32_t pk[16];
+        // pass 2: P = exp2(S*c - m) as bf16 into TMEM over S (16 columns of S
+        // -> 8 columns of packed P).  Masked columns get exponent -inf.
+        {
+          float ls[4] = {0.f, 0.f, 0.f, 0.f};
+          auto expp = [&](const uint32_t (&r)[16], int q) {
+            uint32_t pk[8];
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const int col = pc * 32 + j;
-            const float p0 = (col >= vlo && col < vhi)
-                                 ? ptx::ex2(fmaf(__uint_as_float(r[j]), p.scale_log2, -mm))
-                                 : 0.f;
-            const float p1 = (col + 1 >= vlo && col + 1 < vhi)
-                                 ? ptx::ex2(fmaf(__uint_as_float(r[j + 1]), p.scale_log2, -mm))
-                                 : 0.f;
-            l += p0 + p1;
-            pk[j >> 1] = ptx::pack_bf16x2(p0, p1);
+            for (int j = 0; j < 16; j += 2) {
+              const float x0 = fmaf(__uint_as_float(r[j]), p.scale_log2, -mm);
+              const float x1 = fmaf(__uint_as_float(r[j + 1]), p.scale_log2, -mm);
+              const float e0 = ptx::ex2((uint32_t)(q * 16 + j - vlo) < vspan ? x0 : -INFINITY);
+              const float e1 =
+                  ptx::ex2((uint32_t)(q * 16 + j + 1 - vlo) < vspan ? x1 : -INFINITY);
+              ls[(j >> 1) & 3] += e0 + e1;
+              pk[j >> 1] = ptx::pack_bf16x2(e0, e1);
+            }
+            ptx::tmem_st8(s_addr + q * 8, pk);
+          };
+          const uint32_t zero8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+          // P of piece q lands on S columns [8q, 8q+8): masked pieces below the
+          // live range can be zeroed first (their P columns are below every
+          // live S column); those above only after the live pieces are read
+          for (int q = 0; q < q_lo; ++q) ptx::tmem_st8(s_addr + q * 8, zero8);
+          if (q_lo < q_hi) ptx::tmem_ld16(s_addr + q_lo * 16, bufA);
+          for (int q = q_lo; q < q_hi; q += 2) {
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(bufA);
+            const bool b = q + 1 < q_hi;
+            if (b) ptx::tmem_ld16(s_addr + q * 16 + 16, bufB);
+            expp(bufA, q);
+            if (b) {
+              ptx::tmem_wait_ld();
+              ptx::reg_fence(bufB);
+              if (q + 2 < q_hi) ptx::tmem_ld16(s_addr + q * 16 + 32, bufA);
+              expp(bufB, q + 1);
+            }
           }
-          ptx::tmem_st16(s_addr + pc * 16, pk);
+          for (int q = q_hi; q < nq; ++q) ptx::tmem_st8(s_addr + q * 8, zero8);
+          l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
         }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
@@ -333,11 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       uint8_t* stage = sm.q[slot];
-#pragma unroll 1
-      for (int pc = 0; pc < D / 32; ++pc) {
-        uint32_t r[32];
-        ptx::tmem_ld32(o_addr + pc * 32, r);
-        ptx::tmem_wait_ld();
+      auto emit = [&](const uint32_t (&r)[32], int pc) {
 #pragma unroll
         for (int j8 = 0; j8 < 4; ++j8) {
           uint4 w;
@@ -351,6 +440,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  __uint_as_float(r[8 * j8 + 7]) * inv_l);
           *reinterpret_cast<uint4*>(stage + swz_offset(row, pc * 32 + j8 * 8)) = w;
         }
+      };
+#pragma unroll 1
+      for (int pc = 0; pc < D / 32; ++pc) {
+        uint32_t r0[32];
+        ptx::tmem_ld32(o_addr + pc * 32, r0);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(r0);
+        emit(r0, pc);
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -379,14 +476,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float inv_b = 1.f / (float)p.g.b;
     int tc = 0, kc = 0;
     while (true) {
-      const int slot = tc & 1;
-      ptx::mbar_wait(&sm.q_full[slot], (tc >> 1) & 1, status, 0x40000000u | slot);
+      const int slot = tc % NQ;
+      ptx::mbar_wait(&sm.q_full[slot], (tc / NQ) & 1, status, 0x40000000u | slot);
       const int n = sm.tile_ring[slot];
       if (n < 0) break;
       const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
       {
-        const int st = kc & 1;
-        ptx::mbar_wait(&sm.kv_full[st], (kc >> 1) & 1, status, 0x41000000u | st);
+        const int st = kc % NKV;
+        ptx::mbar_wait(&sm.k_full[st], (kc / NKV) & 1, status, 0x41000000u | st);
+        ptx::mbar_wait(&sm.v_full[st], (kc / NKV) & 1, status, 0x43000000u | st);
         const int nb = p.g.R / p.g.b;
         const int nfull = max(0, min(nb, p.g.Gc - t.blk0));
         for (int lb = 0; lb < nfull; ++lb) {
@@ -425,10 +523,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::named_barrier(2, 128);
         }
-        ptx::fence_proxy_async_global();
         ptx::named_barrier(2, 128);
         if (ptid == 0) {
-          ptx::mbar_arrive(&sm.kv_empty[st]);
+          ptx::mbar_arrive(&sm.k_empty[st]);
+          ptx::mbar_arrive(&sm.v_empty[st]);
           __threadfence();
           ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
         }
@@ -436,9 +534,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int c = 0; c < t.nsc; ++c) {
         if (ptid == 0) {
-          const int st = kc & 1;
-          ptx::mbar_wait(&sm.kv_full[st], (kc >> 1) & 1, status, 0x42000000u | st);
-          ptx::mbar_arrive(&sm.kv_empty[st]);
+          const int st = kc % NKV;
+          ptx::mbar_wait(&sm.k_full[st], (kc / NKV) & 1, status, 0x42000000u | st);
+          ptx::mbar_arrive(&sm.k_empty[st]);
+          ptx::mbar_wait(&sm.v_full[st], (kc / NKV) & 1, status, 0x44000000u | st);
+          ptx::mbar_arrive(&sm.v_empty[st]);
         }
         ++kc;
       }
@@ -466,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D>
+template <int D, int NQ, int NKV, int NS>
 int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
            uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   FwdParams p;
@@ -485,12 +585,14 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
   p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_fwd);
   p.flags_stride = wl.tiles_per_seq;
-  const size_t smem = sizeof(FwdSmem<D>) + 1024;
-  if (cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
+  auto kern = fwd_kernel<D, NQ, NKV, NS>;
+  const size_t smem = sizeof(FwdSmem<D, NQ, NKV, NS>) + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
     return SQB_ERR_LAUNCH;
-  const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
-  fwd_kernel<D><<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.kbar, tm.vbar, p);
+  const int slots = num_sms * ctas_per_sm<NQ, NKV, NS>();
+  const int grid = p.total_tiles < slots ? p.total_tiles : slots;
+  kern<<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.kbar, tm.vbar, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 
@@ -498,8 +600,9 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
 
 int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
                    uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
-  if (pr.D == 64) return launch<64>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
-  if (pr.D == 128) return launch<128>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
+  // single-buffered, two CTAs per SM (measured faster than one double-buffered CTA)
+  if (pr.D == 64) return launch<64, 1, 1, 1>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
+  if (pr.D == 128) return launch<128, 1, 1, 1>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
   return SQB_ERR_UNSUPPORTED;
 }
 

@@ -126,7 +126,8 @@ int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, T
   const int R = sm100::tile_rows(p.b);
   sm100::BwdTensorMaps tm;
   if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) ||
-      !encode_bthd(&tm.v, p, v, R) || !encode_bthd(&tm.dout, p, dout, R) ||
+      !encode_bthd(&tm.v, p, v, R) || !encode_bthd(&tm.o, p, o, R) ||
+      !encode_bthd(&tm.dout, p, dout, R) ||
       !encode_bthd(&tm.dq, p, dq, R) || !encode_bthd(&tm.dk, p, dk, R) ||
       !encode_bthd(&tm.dv, p, dv, R))
     return SQB_ERR_CUDA;

@@ -40,7 +40,7 @@ int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kb
                    uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream);
 
 struct BwdTensorMaps {
-  CUtensorMap q, k, v, dout, dq, dk, dv, kbar, vbar;
+  CUtensorMap q, k, v, o, dout, dq, dk, dv, kbar, vbar;
 };
 
 int launch_backward(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
