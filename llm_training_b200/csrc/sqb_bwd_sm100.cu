@@ -1,9 +1,10 @@
 // sm_100a backward kernel of sqrt-block attention.
 //
-// Persistent, warp-specialised, one CTA per SM (192 threads):
+// Persistent, warp-specialised, one CTA per SM (320 threads):
 //   warp 0      TMA producer + tile scheduler
 //   warp 1      tcgen05.mma issuer and TMEM owner
-//   warps 2-5   softmax-gradient / epilogue, one TMEM lane per thread
+//   warps 2-9   softmax-gradient / epilogue: two warps per TMEM lane quarter,
+//               one TMEM lane (row) per thread, each warp half of the columns
 //
 // A work tile is the same R-row tile as in the forward.  Its chunks are the
 // summary chunks first, then the tile's own (in-block) keys.  Per chunk, with
@@ -51,19 +52,19 @@ struct BwdParams {
 template <int D>
 struct BwdSmem {
   static constexpr int kTileBytes = (D / 64) * kAtomBytes;
-  alignas(1024) uint8_t q[kTileBytes];     // Q, then dQ staging
+  alignas(1024) uint8_t q[kTileBytes];     // Q
   alignas(1024) uint8_t dout[kTileBytes];  // dO
-  alignas(1024) uint8_t k[kTileBytes];     // K chunk, then dK staging
-  alignas(1024) uint8_t v[kTileBytes];     // V chunk, then dV staging
-  alignas(1024) uint8_t p[2 * kAtomBytes];   // O (for delta), then P (128 x 128 keys)
-  alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout)
+  alignas(1024) uint8_t k[kTileBytes];     // K chunk, then dQ staging
+  alignas(1024) uint8_t v[kTileBytes];     // O (for delta), then the V chunk
+  alignas(1024) uint8_t p[2 * kAtomBytes];   // P (128 query rows x 128 keys), then dK staging
+  alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout), then dV staging
   float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
-  uint64_t ld_full, q_empty, kv_full, kv_empty, s_full, ps_full, g_full, g_free;
+  uint64_t ld_full, ld_empty, kv_full, kv_empty, s_full, ps_full, g_full, g_free, delta_done;
   int tile_ring;
   uint32_t tmem_base;
 };
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -95,13 +96,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(&sm.ld_full, 1);
-    ptx::mbar_init(&sm.q_empty, 1);
+    ptx::mbar_init(&sm.ld_empty, 1);
+    ptx::mbar_init(&sm.delta_done, 1);
     ptx::mbar_init(&sm.kv_full, 1);
     ptx::mbar_init(&sm.kv_empty, 1);
     ptx::mbar_init(&sm.s_full, 1);
-    ptx::mbar_init(&sm.ps_full, 4);
+    ptx::mbar_init(&sm.ps_full, 8);
     ptx::mbar_init(&sm.g_full, 1);
-    ptx::mbar_init(&sm.g_free, 4);
+    ptx::mbar_init(&sm.g_free, 8);
     ptx::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -125,12 +127,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Claims one tile ahead and pulls that tile's inputs into L2 while the
+    // current tile runs; Q, dO and O of a tile load as soon as the previous
+    // tile's last MMA has read Q/dO/V (ld_empty), i.e. during its epilogue.
     if (lane == 0) {
+      auto claim = [&]() {
+        const int c = (int)atomicAdd(p.ctrl + kBwdTileCounter, 1u);
+        return c < p.total_tiles ? c : -1;
+      };
+      auto prefetch_rows = [&](const CUtensorMap* m, const Tile& t) {
+#pragma unroll
+        for (int a = 0; a < kAtoms; ++a) ptx::tma_prefetch_l2_4d(m, a * 64, t.h, t.r0, t.n);
+      };
       int tc = 0, kc = 0;
+      int n = claim();
       while (true) {
-        int n = (int)atomicAdd(p.ctrl + kBwdTileCounter, 1u);
-        if (n >= p.total_tiles) n = -1;
-        ptx::mbar_wait(&sm.q_empty, (tc & 1) ^ 1, status, 0x50000000u);
+        if (tc > 0) ptx::mbar_wait(&sm.ld_empty, (tc - 1) & 1, status, 0x50000000u);
         sm.tile_ring = n;
         if (n < 0) {
           ptx::mbar_arrive(&sm.ld_full);
@@ -143,10 +155,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tma_load_4d(sm.q + a * kAtomBytes, &tm_q, &sm.ld_full, a * 64, t.h, t.r0, t.n);
           ptx::tma_load_4d(sm.dout + a * kAtomBytes, &tm_do, &sm.ld_full, a * 64, t.h, t.r0,
                            t.n);
-          ptx::tma_load_4d(sm.p + a * kAtomBytes, &tm_o, &sm.ld_full, a * 64, t.h, t.r0, t.n);
+          ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_o, &sm.ld_full, a * 64, t.h, t.r0, t.n);
+        }
+        prefetch_rows(&tm_k, t);
+        prefetch_rows(&tm_v, t);
+        const int n_next = claim();
+        if (n_next >= 0) {
+          const Tile u = tile_of(n_next);
+          prefetch_rows(&tm_q, u);
+          prefetch_rows(&tm_do, u);
+          prefetch_rows(&tm_o, u);
+          prefetch_rows(&tm_k, u);
+          prefetch_rows(&tm_v, u);
         }
         for (int c = 0; c <= t.nsc; ++c) {
           ptx::mbar_wait(&sm.kv_empty, (kc & 1) ^ 1, status, 0x51000000u);
+          // the first chunk overwrites O in the V buffer: delta must be done
+          if (c == 0) ptx::mbar_wait(&sm.delta_done, tc & 1, status, 0x52000000u);
           if (c < t.nsc) {
             const SumChunk sc = sum_chunk(t, c);
             ptx::mbar_arrive_expect_tx(&sm.kv_full, 2 * kAtoms * kAtomBytes);
@@ -166,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++kc;
         }
         ++tc;
+        n = n_next;
       }
     }
   } else if (warp == 1) {
@@ -210,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
                         (c > 0 || kk > 0) ? 1u : 0u);
           ptx::mma_commit(&sm.g_full);
+          if (c == t.nsc) ptx::mma_commit(&sm.ld_empty);  // Q, dO, V no longer read
           ++kc;
         }
         ++tc;
@@ -217,11 +244,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ gradient warps
-    const int stid = threadIdx.x - 64;  // 0..127
+    // Eight warps, two per TMEM lane quarter: half h = (warp - 2) / 4 takes key
+    // columns [64h, 64h + 64) of S/dP and columns [h*D/2, (h+1)*D/2) of dK, dV
+    // and dQ, so every per-row loop is half as long as with one warp per quarter.
+    const int gtid = threadIdx.x - 64;  // 0..255
+    const int half = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane: query row, then key row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float inv_b = 1.f / (float)p.g.b;
+    constexpr int kHalfD = D / 2;
     int tc = 0, kc = 0;
     while (true) {
       ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x70000000u);
@@ -233,12 +265,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int blk_t = valid ? tq / p.g.b : 0;
       const int lim = valid ? min(blk_t, p.g.Gc) : 0;
       const float L = valid ? p.lse[(size_t)t.bh * p.g.T + tq] * kLog2e : 0.f;
-      float delta = 0.f;  // O was loaded into the P buffer; this row only
+      // delta = rowsum(dO * O); O was loaded into the V buffer.  Both halves
+      // compute the full dot product (cheaper than exchanging halves).
+      float delta = 0.f;
       if (valid) {
 #pragma unroll 4
         for (int cc = 0; cc < D / 8; ++cc) {
           const uint32_t off = swz_offset(row, cc * 8);
-          const uint4 a = *reinterpret_cast<const uint4*>(sm.p + off);
+          const uint4 a = *reinterpret_cast<const uint4*>(sm.v + off);
           const uint4 g = *reinterpret_cast<const uint4*>(sm.dout + off);
           delta += bf16lo(a.x) * bf16lo(g.x) + bf16hi(a.x) * bf16hi(g.x) +
                    bf16lo(a.y) * bf16lo(g.y) + bf16hi(a.y) * bf16hi(g.y) +
@@ -246,24 +280,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                    bf16lo(a.w) * bf16lo(g.w) + bf16hi(a.w) * bf16hi(g.w);
         }
       }
+      // The previous tile's last K/V stage now holds nothing live: its dQ
+      // staging (K buffer) was read by the TMA store, and this tile's O (V
+      // buffer) has been consumed into delta.  Release it to the producer.
+      ptx::named_barrier(1, 256);
+      if (gtid == 0) {
+        ptx::mbar_arrive(&sm.delta_done);
+        if (tc > 0) ptx::mbar_arrive(&sm.kv_empty);
+      }
 
-      // P and dS of one chunk into smem (all 128 key columns; masked -> 0)
+      // P and dS of one chunk into smem (this half's 64 key columns; masked -> 0)
       auto softmax_grad = [&](int N, int vlo, int vhi) {
+        const bool any_col = vhi > vlo;
+        const int wlo = __reduce_min_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
+        const int whi = __reduce_max_sync(0xffffffffu, any_col ? vhi : 0);
         ptx::mbar_wait(&sm.s_full, kc & 1, status, 0x71000000u);
         ptx::tc_fence_after();
 #pragma unroll 1
-        for (int pc = 0; pc < 4; ++pc) {
-          uint32_t s[32], dp[32];
-          const bool live = pc * 32 < N;  // warp-uniform
+        for (int pi = 0; pi < 4; ++pi) {
+          const int c0 = (half * 4 + pi) * 16;  // first of this piece's 16 key columns
+          uint32_t sv[16], dp[16];
+          // warp-uniform: the piece holds a column some row of this warp sees
+          const bool live = c0 < N && c0 < whi && c0 + 16 > wlo;
           if (live) {
-            ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, s);
-            ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, dp);
+            ptx::tmem_ld16(tmem + lane_off + kColS + c0, sv);
+            ptx::tmem_ld16(tmem + lane_off + kColDP + c0, dp);
             ptx::tmem_wait_ld();
-            ptx::reg_fence(s);
+            ptx::reg_fence(sv);
             ptx::reg_fence(dp);
           }
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8) {
+          for (int j8 = 0; j8 < 2; ++j8) {
             uint32_t pw[4], dw[4];
 #pragma unroll
             for (int h2 = 0; h2 < 4; ++h2) {
@@ -271,9 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
                 const int j = j8 * 8 + h2 * 2 + e;
-                const int col = pc * 32 + j;
-                const bool ok = live && col >= vlo && col < vhi;
-                const float pr = ok ? ptx::ex2(fmaf(__uint_as_float(s[j]), p.scale_log2, -L))
+                const bool ok = live && (uint32_t)(c0 + j - vlo) < (uint32_t)(vhi - vlo);
+                const float pr = ok ? ptx::ex2(fmaf(__uint_as_float(sv[j]), p.scale_log2, -L))
                                     : 0.f;
                 pv[e] = pr;
                 dv[e] = ok ? pr * (__uint_as_float(dp[j]) - delta) * p.scale : 0.f;
@@ -281,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               pw[h2] = ptx::pack_bf16x2(pv[0], pv[1]);
               dw[h2] = ptx::pack_bf16x2(dv[0], dv[1]);
             }
-            const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
+            const uint32_t off = swz_offset(row, c0 + j8 * 8);
             *reinterpret_cast<uint4*>(sm.p + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
             *reinterpret_cast<uint4*>(sm.ds + off) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
           }
@@ -298,25 +344,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < t.nsc; ++c) {
         const SumChunk sc = sum_chunk(t, c);
         softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
+        if (gtid == 0) ptx::mbar_arrive(&sm.kv_empty);  // Kbar/Vbar chunk read by all MMAs
         const int j = sc.w + row;  // this lane's summary
         const bool ok = row >= sc.lo - sc.w && row < sc.e - sc.w;
         float* dkrow = p.dkbar + ((size_t)t.bh * p.g.Gc + j) * D;
         float* dvrow = p.dvbar + ((size_t)t.bh * p.g.Gc + j) * D;
 #pragma unroll 1
-        for (int pc = 0; pc < D / 32; ++pc) {
-          uint32_t gv[32], gk[32];
-          ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, gv);
-          ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, gk);
+        for (int pc = 0; pc < kHalfD / 16; ++pc) {
+          const int col0 = half * kHalfD + pc * 16;
+          uint32_t gv[16], gk[16];
+          ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
+          ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
           ptx::tmem_wait_ld();
           ptx::reg_fence(gv);
           ptx::reg_fence(gk);
           if (ok) {
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              ptx::red_add_v4(dvrow + pc * 32 + 4 * j4, __uint_as_float(gv[4 * j4]),
+            for (int j4 = 0; j4 < 4; ++j4) {
+              ptx::red_add_v4(dvrow + col0 + 4 * j4, __uint_as_float(gv[4 * j4]),
                               __uint_as_float(gv[4 * j4 + 1]), __uint_as_float(gv[4 * j4 + 2]),
                               __uint_as_float(gv[4 * j4 + 3]));
-              ptx::red_add_v4(dkrow + pc * 32 + 4 * j4, __uint_as_float(gk[4 * j4]),
+              ptx::red_add_v4(dkrow + col0 + 4 * j4, __uint_as_float(gk[4 * j4]),
                               __uint_as_float(gk[4 * j4 + 1]), __uint_as_float(gk[4 * j4 + 2]),
                               __uint_as_float(gk[4 * j4 + 3]));
             }
@@ -325,7 +373,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&sm.g_free);
-        if (stid == 0) ptx::mbar_arrive(&sm.kv_empty);
         ++kc;
       }
 
@@ -335,50 +382,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       // after the in-block MMAs, so the fence finds the reductions issued
       // during the summary chunks long completed instead of waiting for them.
       __threadfence();
-      ptx::named_barrier(1, 128);
-      if (stid == 0)
+      ptx::named_barrier(1, 256);
+      if (gtid == 0)
         ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
       // every later tile of this sequence has added to the summary sums
-      if (stid < 32)
+      if (gtid < 32)
         ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT, token,
                               status, (uint32_t)n);
-      ptx::named_barrier(1, 128);
+      ptx::named_barrier(1, 256);
       // the summary gradient is block-uniform: stage sum / b of each of the
       // tile's complete blocks in smem once, and re-zero the consumed sums
       const int nfull = max(0, min(p.g.R / p.g.b, p.g.Gc - t.blk0));
       for (int lb = 0; lb < nfull; ++lb) {
         const size_t base = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D;
-        for (int i = stid; i < D; i += 128) {
+        for (int i = gtid; i < D; i += 256) {
           sm.sgrad[0][lb][i] = __ldcg(p.dkbar + base + i) * inv_b;
           sm.sgrad[1][lb][i] = __ldcg(p.dvbar + base + i) * inv_b;
           p.dkbar[base + i] = 0.f;
           p.dvbar[base + i] = 0.f;
         }
       }
-      ptx::named_barrier(1, 128);
+      ptx::named_barrier(1, 256);
       {
         const bool complete = valid && blk_t < p.g.Gc;  // this lane's key is in a full block
         const int lb_t = valid ? blk_t - t.blk0 : 0;
         const float* skrow = sm.sgrad[0][lb_t];
         const float* svrow = sm.sgrad[1][lb_t];
 #pragma unroll 1
-        for (int pc = 0; pc < D / 32; ++pc) {
-          uint32_t gv[32], gk[32];
-          ptx::tmem_ld32(tmem + lane_off + kColS + pc * 32, gv);
-          ptx::tmem_ld32(tmem + lane_off + kColDP + pc * 32, gk);
+        for (int pc = 0; pc < kHalfD / 16; ++pc) {
+          const int col0 = half * kHalfD + pc * 16;
+          uint32_t gv[16], gk[16];
+          ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
+          ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
           ptx::tmem_wait_ld();
           ptx::reg_fence(gv);
           ptx::reg_fence(gk);
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8) {
+          for (int j8 = 0; j8 < 2; ++j8) {
             float fk[8], fv[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               fk[e] = __uint_as_float(gk[8 * j8 + e]);
               fv[e] = __uint_as_float(gv[8 * j8 + e]);
             }
+            const int col = col0 + j8 * 8;
             if (complete) {
-              const int col = pc * 32 + j8 * 8;
               const float4 k0 = *reinterpret_cast<const float4*>(skrow + col);
               const float4 k1 = *reinterpret_cast<const float4*>(skrow + col + 4);
               const float4 v0 = *reinterpret_cast<const float4*>(svrow + col);
@@ -388,11 +436,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               fv[0] += v0.x; fv[1] += v0.y; fv[2] += v0.z; fv[3] += v0.w;
               fv[4] += v1.x; fv[5] += v1.y; fv[6] += v1.z; fv[7] += v1.w;
             }
-            const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
-            *reinterpret_cast<uint4*>(sm.k + off) =
+            const uint32_t off = swz_offset(row, col);
+            *reinterpret_cast<uint4*>(sm.p + off) =
                 make_uint4(ptx::pack_bf16x2(fk[0], fk[1]), ptx::pack_bf16x2(fk[2], fk[3]),
                            ptx::pack_bf16x2(fk[4], fk[5]), ptx::pack_bf16x2(fk[6], fk[7]));
-            *reinterpret_cast<uint4*>(sm.v + off) =
+            *reinterpret_cast<uint4*>(sm.ds + off) =
                 make_uint4(ptx::pack_bf16x2(fv[0], fv[1]), ptx::pack_bf16x2(fv[2], fv[3]),
                            ptx::pack_bf16x2(fv[4], fv[5]), ptx::pack_bf16x2(fv[6], fv[7]));
           }
@@ -401,15 +449,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&sm.g_free);
 #pragma unroll 1
-        for (int pc = 0; pc < D / 32; ++pc) {
-          uint32_t gq[32];
-          ptx::tmem_ld32(tmem + lane_off + kColDQ + pc * 32, gq);
+        for (int pc = 0; pc < kHalfD / 16; ++pc) {
+          const int col0 = half * kHalfD + pc * 16;
+          uint32_t gq[16];
+          ptx::tmem_ld16(tmem + lane_off + kColDQ + col0, gq);
           ptx::tmem_wait_ld();
           ptx::reg_fence(gq);
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8) {
-            const uint32_t off = swz_offset(row, pc * 32 + j8 * 8);
-            *reinterpret_cast<uint4*>(sm.q + off) = make_uint4(
+          for (int j8 = 0; j8 < 2; ++j8) {
+            const uint32_t off = swz_offset(row, col0 + j8 * 8);
+            *reinterpret_cast<uint4*>(sm.k + off) = make_uint4(
                 ptx::pack_bf16x2(__uint_as_float(gq[8 * j8]), __uint_as_float(gq[8 * j8 + 1])),
                 ptx::pack_bf16x2(__uint_as_float(gq[8 * j8 + 2]), __uint_as_float(gq[8 * j8 + 3])),
                 ptx::pack_bf16x2(__uint_as_float(gq[8 * j8 + 4]), __uint_as_float(gq[8 * j8 + 5])),
@@ -418,24 +467,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         ptx::fence_proxy_async_smem();
-        ptx::named_barrier(1, 128);
-        if (stid == 0) {
+        ptx::named_barrier(1, 256);
+        if (gtid == 0) {
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a) {
-            ptx::tma_store_4d(&tm_dk, sm.k + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
-            ptx::tma_store_4d(&tm_dv, sm.v + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
-            ptx::tma_store_4d(&tm_dq, sm.q + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+            ptx::tma_store_4d(&tm_dk, sm.p + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+            ptx::tma_store_4d(&tm_dv, sm.ds + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+            ptx::tma_store_4d(&tm_dq, sm.k + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
           }
           ptx::tma_store_commit();
+          // the staging buffers are rewritten only after this read completes:
+          // P/dS by the next tile's first chunk and K by its first chunk load,
+          // both gated on the kv_empty this thread arrives after its delta
           ptx::tma_store_wait_read_all();
-          ptx::mbar_arrive(&sm.kv_empty);
-          ptx::mbar_arrive(&sm.q_empty);
         }
         ++kc;
       }
       ++tc;
     }
-    if (stid == 0) ptx::tma_store_wait_all();
+    if (gtid == 0) ptx::tma_store_wait_all();
   }
 
   ptx::tc_fence_before();

@@ -143,15 +143,21 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     // ------------------------------------------------------------ producer
     // The whole warp runs the loop (the summary-flag wait is warp-parallel);
     // lane 0 claims tiles and issues every TMA and barrier operation.
+    // Tiles are claimed only when their loads are issued: a claimed tile that
+    // waits to start would publish its summaries late and stall every later
+    // tile of its sequence.
+    auto claim = [&]() {
+      int c = 0;
+      if (lane == 0) {
+        c = (int)atomicAdd(p.ctrl + kFwdTileCounter, 1u);
+        if (c >= p.total_tiles) c = -1;
+      }
+      return __shfl_sync(0xffffffffu, c, 0);
+    };
     int tc = 0, kc = 0;
     while (true) {
       const int slot = tc % NQ;
-      int n = 0;
-      if (lane == 0) {
-        n = (int)atomicAdd(p.ctrl + kFwdTileCounter, 1u);
-        if (n >= p.total_tiles) n = -1;
-      }
-      n = __shfl_sync(0xffffffffu, n, 0);
+      const int n = claim();
       ptx::mbar_wait(&sm.q_empty[slot], ((tc / NQ) & 1) ^ 1, status, 0x10000000u | slot);
       if (lane == 0) {
         sm.tile_ring[slot] = n;
