@@ -353,6 +353,73 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+TRAIN_WORKLOADS = {
+    # name: (config factory kwargs, sequences per GPU, sequence length)
+    "gpt2-small": ("small", 16, 1024),
+    "gpt2-medium-8k": ("medium", 8, 8192),
+}
+
+
+def run_train(args, world, rank, local):
+    """GPT training step (fwd + bwd + clip + fused AdamW, bf16 autocast) with the
+    sqrt-block attention; data-parallel over NCCL when run under torchrun."""
+    from llm_training_b200.config import gpt2_medium, gpt2_small
+    from llm_training_b200.train import Trainer, synthetic_batch
+
+    kind, batch, seq = TRAIN_WORKLOADS[args.workload]
+    cfg = gpt2_small(block_size=seq) if kind == "small" else gpt2_medium(block_size=seq,
+                                                                        sqrt_block_b=96)
+    dev = torch.device("cuda", local)
+    tr = Trainer(cfg, dev, lr=6e-4, weight_decay=0.1, seed=1337, ddp=world > 1)
+    gen = torch.Generator().manual_seed(args.seed * 1000 + rank)
+    x, y = synthetic_batch(gen, batch, seq, cfg.vocab_size, dev)
+    for _ in range(max(args.warmup, 3)):
+        tr.step(x, y)
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            loss, _ = tr.step(x, y)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world) / args.steps
+    tokens = batch * seq * world
+    # end to end: a fresh host batch copied in and the loss read back every step
+    host = [torch.randint(0, cfg.vocab_size, (batch, seq + 1), generator=gen).pin_memory()
+            for _ in range(2)]
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = time.perf_counter()
+    for i in range(max(1, min(args.steps, 5))):
+        tok = host[i % 2].to(dev, non_blocking=True)
+        loss, _ = tr.step(tok[:, :-1], tok[:, 1:])
+        loss.item()
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks((time.perf_counter() - e0) * 1e3, world) / max(1, min(args.steps, 5))
+    if rank == 0:
+        nparams = sum(p.numel() for p in tr.raw_model.parameters())
+        print(json.dumps({
+            "metric": f"{args.workload} train tokens/sec (sqrt-block attention)",
+            "value": round(tokens / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic uniform token ids, seeded per rank",
+            "config": {"workload": args.workload, "model": kind, "params": nparams,
+                       "global_batch": batch * world, "seq_len": seq,
+                       "block": cfg.sqrt_block_b or "default", "parallelism": f"dp{world}",
+                       "optimizer": "fused AdamW lr 6e-4 wd 0.1, clip 1.0"},
+            "e2e": {"value": round(tokens / (e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": batch * (seq + 1) * 8,
+                    "d2h_bytes_per_step": 4},
+            "last_loss": round(float(loss), 4),
+            "clocks": clocks.summary(),
+        }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -364,10 +431,21 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--warmup-seconds", type=float, default=0.5,
                     help="keep warming up at least this long (clock sampler needs samples)")
+    ap.add_argument("--workload", choices=["attn-t16k"] + sorted(TRAIN_WORKLOADS),
+                    default="attn-t16k",
+                    help="attn-t16k: the attention op (default); gpt2-*: a training step")
     args = ap.parse_args()
     world, rank, local = init_dist()
     try:
-        if args.impl == "reference":
+        if args.workload != "attn-t16k":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable":
+                                      "the reference has no implementation of this "
+                                      "attention operator to train with"}), flush=True)
+            else:
+                run_train(args, world, rank, local)
+        elif args.impl == "reference":
             run_reference(args, world, rank)
         else:
             run_ours(args, world, rank, local)

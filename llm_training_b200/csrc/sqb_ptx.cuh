@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers, TMA (cp.async.bulk.tensor,
-// never with .multicast), tcgen05 (alloc / mma / commit / ld / st / fences),
+// plain per-CTA loads only), tcgen05 (alloc / mma / commit / ld / st / fences),
 // UMMA shared-memory and instruction descriptors, and bounded spin waits.
 //
 // Descriptor bit layouts follow the tcgen05 "shared memory descriptor" and

@@ -1,5 +1,5 @@
 // sm_100a (B200) tensor-core kernels for sqrt-block attention: tcgen05.mma with
-// TMEM accumulators, operands staged in shared memory by TMA (no multicast).
+// TMEM accumulators, operands staged in shared memory by plain per-CTA TMA loads.
 #pragma once
 
 #include <cuda.h>

@@ -1,0 +1,78 @@
+"""Synthetic-token GPT training step driving the sqrt-block attention.
+
+This is the op's caller for the training configurations (GPT-2 small at T=1024 on one
+GPU; GPT-2 medium at T=8192 data-parallel over several GPUs).  One step mirrors the
+reference trainer's inner loop (train.py:482-509): bf16-autocast forward and
+cross-entropy (training_utils.py:8-17), backward, clip_grad_norm_(1.0), and AdamW with
+the reference's decay / no-decay parameter groups (training_utils.py:25-51; fused on
+CUDA; weight_decay 0.1, betas (0.9, 0.95) as at train.py:305-306).  With WORLD_SIZE > 1
+the model is wrapped in DistributedDataParallel, whose bucketed NCCL all-reduce of the
+gradients overlaps the backward pass.  Tokens are uniform over the vocabulary from a
+seeded generator: no dataset is involved.
+"""
+
+from __future__ import annotations
+
+import inspect
+
+import torch
+import torch.nn.functional as F
+
+from .model.gpt import GPT
+
+
+def calculate_loss(logits, targets):
+    """Next-token cross-entropy over (B*T, vocab)."""
+    return F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
+
+
+def configure_optimizers(model, weight_decay, learning_rate, betas=(0.9, 0.95),
+                         device_type="cuda"):
+    """AdamW with decay on every >= 2-D parameter and none on the rest."""
+    params = [p for p in model.parameters() if p.requires_grad]
+    decay = [p for p in params if p.dim() >= 2]
+    nodecay = [p for p in params if p.dim() < 2]
+    groups = [{"params": decay, "weight_decay": weight_decay},
+              {"params": nodecay, "weight_decay": 0.0}]
+    fused = "fused" in inspect.signature(torch.optim.AdamW).parameters and device_type == "cuda"
+    return torch.optim.AdamW(groups, lr=learning_rate, betas=betas,
+                             **({"fused": True} if fused else {}))
+
+
+def synthetic_batch(gen, batch, seq, vocab, device):
+    """(x, y) token ids uniform over [0, vocab), y = x shifted by one."""
+    tok = torch.randint(0, vocab, (batch, seq + 1), generator=gen)
+    x, y = tok[:, :-1], tok[:, 1:]
+    if device.type == "cuda":
+        x, y = x.pin_memory(), y.pin_memory()
+    return x.to(device, non_blocking=True), y.to(device, non_blocking=True)
+
+
+class Trainer:
+    """One model + optimizer; ``step(x, y)`` runs forward, backward, clip, AdamW."""
+
+    def __init__(self, config, device, lr=6e-4, weight_decay=0.1, seed=1337, ddp=False,
+                 autocast=True):
+        torch.manual_seed(seed)
+        self.device = device
+        self.model = GPT(config).to(device)
+        self.raw_model = self.model
+        if ddp:
+            from torch.nn.parallel import DistributedDataParallel
+
+            ids = [device.index] if device.type == "cuda" else None
+            self.model = DistributedDataParallel(self.model, device_ids=ids)
+        self.optimizer = configure_optimizers(self.raw_model, weight_decay, lr,
+                                              device_type=device.type)
+        self.autocast = autocast and device.type == "cuda"
+
+    def step(self, x, y):
+        self.optimizer.zero_grad(set_to_none=True)
+        with torch.autocast(device_type=self.device.type, dtype=torch.bfloat16,
+                            enabled=self.autocast):
+            logits = self.model(x)
+            loss = calculate_loss(logits, y)
+        loss.backward()
+        norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), 1.0)
+        self.optimizer.step()
+        return loss.detach(), norm
