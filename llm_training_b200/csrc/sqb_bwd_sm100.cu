@@ -20,9 +20,11 @@
 // its block - before storing dK, dV and dQ through smem with TMA.
 //
 // The summary gradient of block j is complete once every later tile has
-// added to it.  Tiles are handed out in descending sequence order; each tile
-// sets flag[s] once its own additions are done, and before reading its blocks'
-// sums checks (32 flags at a time) that every later tile has set its flag.
+// added to it.  Tiles are handed out in descending sequence order.  Each of a
+// tile's 256 gradient threads adds 1 to the tile's counter with release
+// semantics once its own additions are issued, so the counter reaches 256 per
+// launch; before reading its blocks' sums a tile checks (32 counters at a
+// time) that every later tile's counter has reached 256 * (launch epoch).
 // The reader re-zeroes the sums it consumed, so the accumulators are zero
 // again when the kernel ends.  Waits are bounded like the forward's.
 
@@ -376,19 +378,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kc;
       }
 
+      // ---- publish: each of the 256 gradient threads bumps this tile's counter
+      // with release semantics after its own reductions, so no fence or barrier
+      // is needed; a counter at 256 * token means the tile's additions landed
+      ptx::red_release_add(p.flags + (size_t)t.bh * p.flags_stride + t.s, 1u);
+
       // ---- in-block chunk
       softmax_grad(t.n_in, valid ? blk_t * p.g.b - t.r0 : 0, valid ? row + 1 : 0);
-      // ---- publish this tile's summary-gradient additions.  Done only now,
-      // after the in-block MMAs, so the fence finds the reductions issued
-      // during the summary chunks long completed instead of waiting for them.
-      __threadfence();
-      ptx::named_barrier(1, 256);
-      if (gtid == 0)
-        ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
       // every later tile of this sequence has added to the summary sums
       if (gtid < 32)
-        ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT, token,
-                              status, (uint32_t)n);
+        ptx::counters_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT,
+                                 256u * token, status, (uint32_t)n);
       ptx::named_barrier(1, 256);
       // the summary gradient is block-uniform: stage sum / b of each of the
       // tile's complete blocks in smem once, and re-zero the consumed sums

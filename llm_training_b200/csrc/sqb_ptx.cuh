@@ -169,6 +169,48 @@ __device__ __forceinline__ bool flags_wait_range(const uint32_t* flags, int lo, 
   return done;
 }
 
+// Release increment: every memory operation this thread issued before it is
+// visible to whoever acquires a value that includes the increment.
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Warp-collective: spins until every counter in [lo, hi) is >= want; otherwise
+// as flags_wait_range.
+__device__ __forceinline__ bool counters_wait_range(const uint32_t* ctr, int lo, int hi,
+                                                    uint32_t want, uint32_t* status,
+                                                    uint32_t detail) {
+  const int lane = threadIdx.x & 31;
+  uint64_t t0 = 0;
+  bool timed = false;
+  bool done = false;
+  while (true) {
+    bool ok = true;
+    for (int i = lo + lane; i < hi; i += 32) ok &= (ld_acquire_gpu(ctr + i) >= want);
+    if (__all_sync(0xffffffffu, ok)) {
+      done = true;
+      break;
+    }
+    int stop = 0;
+    if (lane == 0) {
+      if (!timed) {
+        t0 = globaltimer();
+        timed = true;
+      }
+      if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {
+        stop = 1;
+      } else if (globaltimer() - t0 > kWaitBudgetNs) {
+        record_status(status, SQB_ERR_TIMEOUT, detail);
+        stop = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, stop, 0)) break;
+    __nanosleep(40);
+  }
+  __syncwarp();
+  return done;
+}
+
 // Fire-and-forget fp32 vector add into global memory (no value returned).
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
   asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a),
