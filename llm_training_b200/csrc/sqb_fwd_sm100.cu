@@ -143,9 +143,11 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     // ------------------------------------------------------------ producer
     // The whole warp runs the loop (the summary-flag wait is warp-parallel);
     // lane 0 claims tiles and issues every TMA and barrier operation.
-    // Tiles are claimed only when their loads are issued: a claimed tile that
-    // waits to start would publish its summaries late and stall every later
-    // tile of its sequence.
+    // Tiles are claimed only once their Q slot is free and their loads can be
+    // issued: a claimed tile that waits to start would publish its summaries
+    // late and stall every later tile of its sequence.  (Measured: claiming
+    // before the slot wait, or prefetching the likely next tile into L2, are
+    // both slower.)
     auto claim = [&]() {
       int c = 0;
       if (lane == 0) {
@@ -157,8 +159,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     int tc = 0, kc = 0;
     while (true) {
       const int slot = tc % NQ;
-      const int n = claim();
       ptx::mbar_wait(&sm.q_empty[slot], ((tc / NQ) & 1) ^ 1, status, 0x10000000u | slot);
+      const int n = claim();
       if (lane == 0) {
         sm.tile_ring[slot] = n;
         if (n < 0) ptx::mbar_arrive(&sm.q_full[slot]);
@@ -489,53 +491,48 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
       {
         const int st = kc % NKV;
-        ptx::mbar_wait(&sm.k_full[st], (kc / NKV) & 1, status, 0x41000000u | st);
-        ptx::mbar_wait(&sm.v_full[st], (kc / NKV) & 1, status, 0x43000000u | st);
         const int nb = p.g.R / p.g.b;
         const int nfull = max(0, min(nb, p.g.Gc - t.blk0));
-        for (int lb = 0; lb < nfull; ++lb) {
-          float ak[8], av[8];
+        // K then V: each buffer is released as soon as its own sums are read,
+        // so the summary chunk's Kbar load can start while V is still pooled.
+#pragma unroll 1
+        for (int kv = 0; kv < 2; ++kv) {
+          ptx::mbar_wait(kv == 0 ? &sm.k_full[st] : &sm.v_full[st], (kc / NKV) & 1, status,
+                         (kv == 0 ? 0x41000000u : 0x43000000u) | st);
+          const uint8_t* buf = kv == 0 ? sm.k[st] : sm.v[st];
+          __nv_bfloat16* dst = kv == 0 ? p.kbar : p.vbar;
+          for (int lb = 0; lb < nfull; ++lb) {
+            float a[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) ak[j] = av[j] = 0.f;
-          if (cc < D / 8) {
-            for (int i = 0; i < p.g.b / 8; ++i) {
-              const int r = lb * p.g.b + rg + 8 * i;
-              const uint32_t off = swz_offset(r, cc * 8);
-              add_bf16x8(ak, *reinterpret_cast<const uint4*>(sm.k[st] + off));
-              add_bf16x8(av, *reinterpret_cast<const uint4*>(sm.v[st] + off));
+            for (int j = 0; j < 8; ++j) a[j] = 0.f;
+            if (cc < D / 8) {
+              for (int i = 0; i < p.g.b / 8; ++i) {
+                const int r = lb * p.g.b + rg + 8 * i;
+                add_bf16x8(a, *reinterpret_cast<const uint4*>(buf + swz_offset(r, cc * 8)));
+              }
             }
-          }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            ak[j] += __shfl_xor_sync(0xffffffffu, ak[j], 16);
-            av[j] += __shfl_xor_sync(0xffffffffu, av[j], 16);
-          }
-          if ((ptid & 16) == 0 && cc < D / 8) {
+            for (int j = 0; j < 8; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], 16);
+            if ((ptid & 16) == 0 && cc < D / 8) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              sm.red[pw][0][cc * 8 + j] = ak[j];
-              sm.red[pw][1][cc * 8 + j] = av[j];
+              for (int j = 0; j < 8; ++j) sm.red[pw][kv][cc * 8 + j] = a[j];
             }
+            ptx::named_barrier(2, 128);
+            if (ptid < D) {
+              const float sum = sm.red[0][kv][ptid] + sm.red[1][kv][ptid] +
+                                sm.red[2][kv][ptid] + sm.red[3][kv][ptid];
+              dst[((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D + ptid] =
+                  __float2bfloat16_rn(sum * inv_b);
+            }
+            ptx::named_barrier(2, 128);
           }
           ptx::named_barrier(2, 128);
-          if (ptid < D) {
-            const float sk = sm.red[0][0][ptid] + sm.red[1][0][ptid] + sm.red[2][0][ptid] +
-                             sm.red[3][0][ptid];
-            const float sv = sm.red[0][1][ptid] + sm.red[1][1][ptid] + sm.red[2][1][ptid] +
-                             sm.red[3][1][ptid];
-            const size_t off = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D + ptid;
-            p.kbar[off] = __float2bfloat16_rn(sk * inv_b);
-            p.vbar[off] = __float2bfloat16_rn(sv * inv_b);
-          }
-          ptx::named_barrier(2, 128);
+          if (ptid == 0) ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st] : &sm.v_empty[st]);
         }
-        ptx::named_barrier(2, 128);
-        if (ptid == 0) {
-          ptx::mbar_arrive(&sm.k_empty[st]);
-          ptx::mbar_arrive(&sm.v_empty[st]);
-          __threadfence();
-          ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
-        }
+        // The barrier above orders every pooling thread's summary writes
+        // before this release store, which makes them visible to any CTA that
+        // acquires the flag.
+        if (ptid == 0) ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
         ++kc;
       }
       for (int c = 0; c < t.nsc; ++c) {
