@@ -129,22 +129,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Claims one tile ahead and pulls that tile's inputs into L2 while the
-    // current tile runs; Q, dO and O of a tile load as soon as the previous
-    // tile's last MMA has read Q/dO/V (ld_empty), i.e. during its epilogue.
+    // A tile is claimed when its loads can be issued: Q, dO and O of a tile
+    // load as soon as the previous tile's last MMA has read Q/dO/V
+    // (ld_empty), i.e. during its epilogue.  A tile claimed earlier would
+    // hold back every tile of its sequence that waits for its summary
+    // gradients (measured: claiming one tile ahead, with or without an L2
+    // prefetch of its inputs, is slower).
     if (lane == 0) {
       auto claim = [&]() {
         const int c = (int)atomicAdd(p.ctrl + kBwdTileCounter, 1u);
         return c < p.total_tiles ? c : -1;
       };
-      auto prefetch_rows = [&](const CUtensorMap* m, const Tile& t) {
-#pragma unroll
-        for (int a = 0; a < kAtoms; ++a) ptx::tma_prefetch_l2_4d(m, a * 64, t.h, t.r0, t.n);
-      };
       int tc = 0, kc = 0;
-      int n = claim();
       while (true) {
         if (tc > 0) ptx::mbar_wait(&sm.ld_empty, (tc - 1) & 1, status, 0x50000000u);
+        const int n = claim();
         sm.tile_ring = n;
         if (n < 0) {
           ptx::mbar_arrive(&sm.ld_full);
@@ -158,17 +157,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tma_load_4d(sm.dout + a * kAtomBytes, &tm_do, &sm.ld_full, a * 64, t.h, t.r0,
                            t.n);
           ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_o, &sm.ld_full, a * 64, t.h, t.r0, t.n);
-        }
-        prefetch_rows(&tm_k, t);
-        prefetch_rows(&tm_v, t);
-        const int n_next = claim();
-        if (n_next >= 0) {
-          const Tile u = tile_of(n_next);
-          prefetch_rows(&tm_q, u);
-          prefetch_rows(&tm_do, u);
-          prefetch_rows(&tm_o, u);
-          prefetch_rows(&tm_k, u);
-          prefetch_rows(&tm_v, u);
         }
         for (int c = 0; c <= t.nsc; ++c) {
           ptx::mbar_wait(&sm.kv_empty, (kc & 1) ^ 1, status, 0x51000000u);
@@ -193,7 +181,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++kc;
         }
         ++tc;
-        n = n_next;
       }
     }
   } else if (warp == 1) {
