@@ -1,10 +1,11 @@
 // sm_100a backward kernel of sqrt-block attention.
 //
-// Persistent, warp-specialised, one CTA per SM (320 threads):
+// Persistent, warp-specialised, one CTA per SM (352 threads):
 //   warp 0      TMA producer + tile scheduler
 //   warp 1      tcgen05.mma issuer and TMEM owner
 //   warps 2-9   softmax-gradient / epilogue: two warps per TMEM lane quarter,
 //               one TMEM lane (row) per thread, each warp half of the columns
+//   warp 10     publisher of the summary-gradient counters
 //
 // A work tile is the same R-row tile as in the forward.  Its chunks are the
 // summary chunks first, then the tile's own (in-block) keys.  Per chunk, with
@@ -20,11 +21,11 @@
 // its block - before storing dK, dV and dQ through smem with TMA.
 //
 // The summary gradient of block j is complete once every later tile has
-// added to it.  Tiles are handed out in descending sequence order.  Each of a
-// tile's 256 gradient threads adds 1 to the tile's counter with release
-// semantics once its own additions are issued, so the counter reaches 256 per
-// launch; before reading its blocks' sums a tile checks (32 counters at a
-// time) that every later tile's counter has reached 256 * (launch epoch).
+// added to it.  Tiles are handed out in descending sequence order.  Once
+// every gradient warp of a tile has issued its additions, the publisher warp
+// adds 1 to the tile's counter with release semantics, so the counter reaches
+// the launch epoch; before reading its blocks' sums a tile checks (32
+// counters at a time) that every later tile's counter has reached it.
 // The reader re-zeroes the sums it consumed, so the accumulators are zero
 // again when the kernel ends.  Waits are bounded like the forward's.
 
@@ -62,11 +63,12 @@ struct BwdSmem {
   alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout), then dV staging
   float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
   uint64_t ld_full, ld_empty, kv_full, kv_empty, s_full, ps_full, g_full, g_free, delta_done;
+  uint64_t red_done, pub_read;
   int tile_ring;
   uint32_t tmem_base;
 };
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -100,6 +102,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(&sm.ld_full, 1);
     ptx::mbar_init(&sm.ld_empty, 1);
     ptx::mbar_init(&sm.delta_done, 1);
+    ptx::mbar_init(&sm.red_done, 8);  // one arrive per gradient warp
+    ptx::mbar_init(&sm.pub_read, 1);
     ptx::mbar_init(&sm.kv_full, 1);
     ptx::mbar_init(&sm.kv_empty, 1);
     ptx::mbar_init(&sm.s_full, 1);
@@ -142,7 +146,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int tc = 0, kc = 0;
       while (true) {
-        if (tc > 0) ptx::mbar_wait(&sm.ld_empty, (tc - 1) & 1, status, 0x50000000u);
+        if (tc > 0) {
+          ptx::mbar_wait(&sm.ld_empty, (tc - 1) & 1, status, 0x50000000u);
+          ptx::mbar_wait(&sm.pub_read, (tc - 1) & 1, status, 0x53000000u);
+        }
         const int n = claim();
         sm.tile_ring = n;
         if (n < 0) {
@@ -231,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++tc;
       }
     }
-  } else {
+  } else if (warp < 10) {
     // ------------------------------------------------------------ gradient warps
     // Eight warps, two per TMEM lane quarter: half h = (warp - 2) / 4 takes key
     // columns [64h, 64h + 64) of S/dP and columns [h*D/2, (h+1)*D/2) of dK, dV
@@ -365,17 +372,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kc;
       }
 
-      // ---- publish: each of the 256 gradient threads bumps this tile's counter
-      // with release semantics after its own reductions, so no fence or barrier
-      // is needed; a counter at 256 * token means the tile's additions landed
-      ptx::red_release_add(p.flags + (size_t)t.bh * p.flags_stride + t.s, 1u);
+      // ---- publish (by the publisher warp): this warp's additions are done
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&sm.red_done);
 
       // ---- in-block chunk
       softmax_grad(t.n_in, valid ? blk_t * p.g.b - t.r0 : 0, valid ? row + 1 : 0);
       // every later tile of this sequence has added to the summary sums
       if (gtid < 32)
         ptx::counters_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT,
-                                 256u * token, status, (uint32_t)n);
+                                 token, status, (uint32_t)n);
       ptx::named_barrier(1, 256);
       // the summary gradient is block-uniform: stage sum / b of each of the
       // tile's complete blocks in smem once, and re-zero the consumed sums
@@ -473,6 +479,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++tc;
     }
     if (gtid == 0) ptx::tma_store_wait_all();
+  } else {
+    // ------------------------------------------------------------ publisher
+    // Makes a tile's summary-gradient additions visible to other CTAs.  The
+    // gradient warps arrive on red_done after their last addition (the
+    // arrive orders them at CTA scope); this lane's release add at GPU scope
+    // then covers them for any CTA that acquires the counter, which reaches
+    // token once per launch.  The release waits until every outstanding
+    // addition is acknowledged, so it is kept off the gradient warps.
+    if (lane == 0) {
+      int tc = 0;
+      while (true) {
+        ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x80000000u);
+        const int n = sm.tile_ring;
+        ptx::mbar_arrive(&sm.pub_read);  // the producer may now rewrite tile_ring
+        if (n < 0) break;
+        const Tile t = tile_of(n);
+        ptx::mbar_wait(&sm.red_done, tc & 1, status, 0x81000000u);
+        ptx::red_release_add(p.flags + (size_t)t.bh * p.flags_stride + t.s, 1u);
+        ++tc;
+      }
+    }
   }
 
   ptx::tc_fence_before();
