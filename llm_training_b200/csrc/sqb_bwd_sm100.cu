@@ -63,7 +63,7 @@ struct BwdSmem {
   alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout), then dV staging
   float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
   uint64_t ld_full, ld_empty, kv_full, kv_empty, s_full, ps_full, g_full, g_free, delta_done;
-  uint64_t red_done, pub_read;
+  uint64_t red_done, pub_read, sums_ready, sgrad_free;
   int tile_ring;
   uint32_t tmem_base;
 };
@@ -104,6 +104,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(&sm.delta_done, 1);
     ptx::mbar_init(&sm.red_done, 8);  // one arrive per gradient warp
     ptx::mbar_init(&sm.pub_read, 1);
+    ptx::mbar_init(&sm.sums_ready, 1);
+    ptx::mbar_init(&sm.sgrad_free, 8);  // one arrive per gradient warp
     ptx::mbar_init(&sm.kv_full, 1);
     ptx::mbar_init(&sm.kv_empty, 1);
     ptx::mbar_init(&sm.s_full, 1);
@@ -248,7 +250,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane: query row, then key row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const float inv_b = 1.f / (float)p.g.b;
     constexpr int kHalfD = D / 2;
     int tc = 0, kc = 0;
     while (true) {
@@ -378,24 +379,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- in-block chunk
       softmax_grad(t.n_in, valid ? blk_t * p.g.b - t.r0 : 0, valid ? row + 1 : 0);
-      // every later tile of this sequence has added to the summary sums
-      if (gtid < 32)
-        ptx::counters_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT,
-                                 token, status, (uint32_t)n);
-      ptx::named_barrier(1, 256);
-      // the summary gradient is block-uniform: stage sum / b of each of the
-      // tile's complete blocks in smem once, and re-zero the consumed sums
-      const int nfull = max(0, min(p.g.R / p.g.b, p.g.Gc - t.blk0));
-      for (int lb = 0; lb < nfull; ++lb) {
-        const size_t base = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D;
-        for (int i = gtid; i < D; i += 256) {
-          sm.sgrad[0][lb][i] = __ldcg(p.dkbar + base + i) * inv_b;
-          sm.sgrad[1][lb][i] = __ldcg(p.dvbar + base + i) * inv_b;
-          p.dkbar[base + i] = 0.f;
-          p.dvbar[base + i] = 0.f;
-        }
-      }
-      ptx::named_barrier(1, 256);
+      // the publisher has staged sum / b of the tile's complete blocks
+      ptx::mbar_wait(&sm.sums_ready, tc & 1, status, 0x73000000u);
       {
         const bool complete = valid && blk_t < p.g.Gc;  // this lane's key is in a full block
         const int lb_t = valid ? blk_t - t.blk0 : 0;
@@ -440,7 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+        if (lane == 0) {
+          ptx::mbar_arrive(&sm.g_free);
+          ptx::mbar_arrive(&sm.sgrad_free);
+        }
 #pragma unroll 1
         for (int pc = 0; pc < kHalfD / 16; ++pc) {
           const int col0 = half * kHalfD + pc * 16;
@@ -481,24 +469,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (gtid == 0) ptx::tma_store_wait_all();
   } else {
     // ------------------------------------------------------------ publisher
-    // Makes a tile's summary-gradient additions visible to other CTAs.  The
-    // gradient warps arrive on red_done after their last addition (the
-    // arrive orders them at CTA scope); this lane's release add at GPU scope
-    // then covers them for any CTA that acquires the counter, which reaches
-    // token once per launch.  The release waits until every outstanding
-    // addition is acknowledged, so it is kept off the gradient warps.
-    if (lane == 0) {
-      int tc = 0;
-      while (true) {
-        ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x80000000u);
-        const int n = sm.tile_ring;
-        ptx::mbar_arrive(&sm.pub_read);  // the producer may now rewrite tile_ring
-        if (n < 0) break;
-        const Tile t = tile_of(n);
-        ptx::mbar_wait(&sm.red_done, tc & 1, status, 0x81000000u);
-        ptx::red_release_add(p.flags + (size_t)t.bh * p.flags_stride + t.s, 1u);
-        ++tc;
+    // Per tile: (1) makes the tile's summary-gradient additions visible to
+    // other CTAs.  The gradient warps arrive on red_done after their last
+    // addition (the arrive orders them at CTA scope); lane 0's release add at
+    // GPU scope then covers them for any CTA that acquires the counter, which
+    // reaches token once per launch.  The release waits until every
+    // outstanding addition is acknowledged, so it is kept off the gradient
+    // warps.  (2) Waits until every later tile of the sequence has published,
+    // stages sum / b of each of the tile's complete blocks in smem for the
+    // gradient warps' epilogue (sums_ready), and re-zeroes the consumed sums.
+    const float inv_b = 1.f / (float)p.g.b;
+    int tc = 0;
+    while (true) {
+      ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x80000000u);
+      const int n = sm.tile_ring;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&sm.pub_read);  // the producer may rewrite tile_ring
+      if (n < 0) break;
+      const Tile t = tile_of(n);
+      ptx::mbar_wait(&sm.red_done, tc & 1, status, 0x81000000u);
+      if (lane == 0) ptx::red_release_add(p.flags + (size_t)t.bh * p.flags_stride + t.s, 1u);
+      ptx::counters_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT, token,
+                               status, (uint32_t)n);
+      if (tc > 0) ptx::mbar_wait(&sm.sgrad_free, (tc - 1) & 1, status, 0x82000000u);
+      const int nfull = max(0, min(p.g.R / p.g.b, p.g.Gc - t.blk0));
+      for (int lb = 0; lb < nfull; ++lb) {
+        const size_t base = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D;
+        for (int i = lane * 4; i < D; i += 128) {
+          const float4 k4 = __ldcg(reinterpret_cast<const float4*>(p.dkbar + base + i));
+          const float4 v4 = __ldcg(reinterpret_cast<const float4*>(p.dvbar + base + i));
+          *reinterpret_cast<float4*>(&sm.sgrad[0][lb][i]) =
+              make_float4(k4.x * inv_b, k4.y * inv_b, k4.z * inv_b, k4.w * inv_b);
+          *reinterpret_cast<float4*>(&sm.sgrad[1][lb][i]) =
+              make_float4(v4.x * inv_b, v4.y * inv_b, v4.z * inv_b, v4.w * inv_b);
+          *reinterpret_cast<float4*>(p.dkbar + base + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(p.dvbar + base + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&sm.sums_ready);
+      ++tc;
     }
   }
 
