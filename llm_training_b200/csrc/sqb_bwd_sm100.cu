@@ -62,7 +62,8 @@ struct BwdSmem {
   alignas(1024) uint8_t p[2 * kAtomBytes];   // P (128 query rows x 128 keys), then dK staging
   alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout), then dV staging
   float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
-  uint64_t ld_full, ld_empty, kv_full, kv_empty, s_full, ps_full, g_full, g_free, delta_done;
+  uint64_t ld_full, ld_empty, k_full, k_empty, v_full, v_empty, s_full, ps_full, g_full, g_free;
+  uint64_t delta_done, stage_free;
   uint64_t red_done, pub_read, sums_ready, sgrad_free;
   int tile_ring;
   uint32_t tmem_base;
@@ -106,8 +107,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(&sm.pub_read, 1);
     ptx::mbar_init(&sm.sums_ready, 1);
     ptx::mbar_init(&sm.sgrad_free, 8);  // one arrive per gradient warp
-    ptx::mbar_init(&sm.kv_full, 1);
-    ptx::mbar_init(&sm.kv_empty, 1);
+    ptx::mbar_init(&sm.k_full, 1);
+    ptx::mbar_init(&sm.k_empty, 1);  // dQ MMA of the chunk complete
+    ptx::mbar_init(&sm.v_full, 1);
+    ptx::mbar_init(&sm.v_empty, 1);  // dP MMA of the chunk complete
+    ptx::mbar_init(&sm.stage_free, 1);
     ptx::mbar_init(&sm.s_full, 1);
     ptx::mbar_init(&sm.ps_full, 8);
     ptx::mbar_init(&sm.g_full, 1);
@@ -167,25 +171,57 @@ __global__ void __launch_bounds__(kThreads, 1)
                            t.n);
           ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_o, &sm.ld_full, a * 64, t.h, t.r0, t.n);
         }
+        // K and V buffers are refilled independently: V as soon as the
+        // previous chunk's dP has read it, K once its dQ has (the MMA warp
+        // issues dQ first among a chunk's gradient MMAs).  A tile's first K
+        // load also waits for the previous tile's dQ staging in the K buffer
+        // to be read by its TMA store; its first V load waits for delta,
+        // which reads O from the V buffer.
         for (int c = 0; c <= t.nsc; ++c) {
-          ptx::mbar_wait(&sm.kv_empty, (kc & 1) ^ 1, status, 0x51000000u);
-          // the first chunk overwrites O in the V buffer: delta must be done
-          if (c == 0) ptx::mbar_wait(&sm.delta_done, tc & 1, status, 0x52000000u);
-          if (c < t.nsc) {
-            const SumChunk sc = sum_chunk(t, c);
-            ptx::mbar_arrive_expect_tx(&sm.kv_full, 2 * kAtoms * kAtomBytes);
+          auto load_k = [&]() {
+            ptx::mbar_wait(&sm.k_empty, (kc & 1) ^ 1, status, 0x51000000u);
+            if (c == 0 && tc > 0)
+              ptx::mbar_wait(&sm.stage_free, (tc - 1) & 1, status, 0x54000000u);
+            if (c < t.nsc) {
+              const SumChunk sc = sum_chunk(t, c);
+              ptx::mbar_arrive_expect_tx(&sm.k_full, kAtoms * kAtomBytes);
 #pragma unroll
-            for (int a = 0; a < kAtoms; ++a) {
-              ptx::tma_load_3d(sm.k + a * kAtomBytes, &tm_kbar, &sm.kv_full, a * 64, sc.w, t.bh);
-              ptx::tma_load_3d(sm.v + a * kAtomBytes, &tm_vbar, &sm.kv_full, a * 64, sc.w, t.bh);
+              for (int a = 0; a < kAtoms; ++a)
+                ptx::tma_load_3d(sm.k + a * kAtomBytes, &tm_kbar, &sm.k_full, a * 64, sc.w, t.bh);
+            } else {
+              ptx::mbar_arrive_expect_tx(&sm.k_full, kAtoms * box_bytes);
+#pragma unroll
+              for (int a = 0; a < kAtoms; ++a)
+                ptx::tma_load_4d(sm.k + a * kAtomBytes, &tm_k, &sm.k_full, a * 64, t.h, t.r0,
+                                 t.n);
             }
+          };
+          auto load_v = [&]() {
+            ptx::mbar_wait(&sm.v_empty, (kc & 1) ^ 1, status, 0x55000000u);
+            if (c == 0) ptx::mbar_wait(&sm.delta_done, tc & 1, status, 0x52000000u);
+            if (c < t.nsc) {
+              const SumChunk sc = sum_chunk(t, c);
+              ptx::mbar_arrive_expect_tx(&sm.v_full, kAtoms * kAtomBytes);
+#pragma unroll
+              for (int a = 0; a < kAtoms; ++a)
+                ptx::tma_load_3d(sm.v + a * kAtomBytes, &tm_vbar, &sm.v_full, a * 64, sc.w, t.bh);
+            } else {
+              ptx::mbar_arrive_expect_tx(&sm.v_full, kAtoms * box_bytes);
+#pragma unroll
+              for (int a = 0; a < kAtoms; ++a)
+                ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_v, &sm.v_full, a * 64, t.h, t.r0,
+                                 t.n);
+            }
+          };
+          // in the order their buffers free up: for a tile's first chunk K
+          // (previous tile's store read) before V (this tile's delta), for
+          // later chunks V (previous dP) before K (previous dQ)
+          if (c == 0) {
+            load_k();
+            load_v();
           } else {
-            ptx::mbar_arrive_expect_tx(&sm.kv_full, 2 * kAtoms * box_bytes);
-#pragma unroll
-            for (int a = 0; a < kAtoms; ++a) {
-              ptx::tma_load_4d(sm.k + a * kAtomBytes, &tm_k, &sm.kv_full, a * 64, t.h, t.r0, t.n);
-              ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_v, &sm.kv_full, a * 64, t.h, t.r0, t.n);
-            }
+            load_v();
+            load_k();
           }
           ++kc;
         }
@@ -209,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kq = round16(t.rows) / 16;  // k-steps over query rows
         for (int c = 0; c <= t.nsc; ++c) {
           const int N = c < t.nsc ? sum_chunk(t, c).n16 : t.n_in;
-          ptx::mbar_wait(&sm.kv_full, kc & 1, status, 0x61000000u);
+          ptx::mbar_wait(&sm.k_full, kc & 1, status, 0x61000000u);
           if (kc > 0) ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
           ptx::tc_fence_after();
           const uint32_t idesc_s = ptx::idesc_bf16(128, N, false, false);
@@ -217,22 +253,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < D / 16; ++kk)
             ptx::mma_ss(tmem + kColS, desc_kmajor(q_s, kk), desc_kmajor(k_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
+          ptx::mbar_wait(&sm.v_full, kc & 1, status, 0x64000000u);
+          ptx::tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             ptx::mma_ss(tmem + kColDP, desc_kmajor(do_s, kk), desc_kmajor(v_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
           ptx::mma_commit(&sm.s_full);
+          ptx::mma_commit(&sm.v_empty);  // the V chunk is read only by dP
           ptx::mbar_wait(&sm.ps_full, kc & 1, status, 0x63000000u);
           ptx::tc_fence_after();
+          for (int kk = 0; kk < N / 16; ++kk)  // dQ += dS Kc (first: frees the K buffer)
+            ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
+                        (c > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_commit(&sm.k_empty);
           for (int kk = 0; kk < kq; ++kk)  // dVc = P^T dO
             ptx::mma_ss(tmem + kColS, desc_mnmajor(p_s, kk), desc_mnmajor(do_s, kk), idesc_dvdk,
                         kk > 0 ? 1u : 0u);
           for (int kk = 0; kk < kq; ++kk)  // dKc = dS^T Q
             ptx::mma_ss(tmem + kColDP, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
                         kk > 0 ? 1u : 0u);
-          for (int kk = 0; kk < N / 16; ++kk)  // dQ += dS Kc
-            ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
-                        (c > 0 || kk > 0) ? 1u : 0u);
           ptx::mma_commit(&sm.g_full);
           if (c == t.nsc) ptx::mma_commit(&sm.ld_empty);  // Q, dO, V no longer read
           ++kc;
@@ -277,14 +317,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                    bf16lo(a.w) * bf16lo(g.w) + bf16hi(a.w) * bf16hi(g.w);
         }
       }
-      // The previous tile's last K/V stage now holds nothing live: its dQ
-      // staging (K buffer) was read by the TMA store, and this tile's O (V
-      // buffer) has been consumed into delta.  Release it to the producer.
+      // This tile's O (V buffer) has been consumed into delta: the first V
+      // chunk may be loaded.  The barrier also orders this tile's P/dS writes
+      // after gtid 0's wait for the previous tile's staging stores.
       ptx::named_barrier(1, 256);
-      if (gtid == 0) {
-        ptx::mbar_arrive(&sm.delta_done);
-        if (tc > 0) ptx::mbar_arrive(&sm.kv_empty);
-      }
+      if (gtid == 0) ptx::mbar_arrive(&sm.delta_done);
 
       // P and dS of one chunk into smem (this half's 64 key columns; masked -> 0)
       auto softmax_grad = [&](int N, int vlo, int vhi) {
@@ -341,7 +378,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < t.nsc; ++c) {
         const SumChunk sc = sum_chunk(t, c);
         softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
-        if (gtid == 0) ptx::mbar_arrive(&sm.kv_empty);  // Kbar/Vbar chunk read by all MMAs
         const int j = sc.w + row;  // this lane's summary
         const bool ok = row >= sc.lo - sc.w && row < sc.e - sc.w;
         float* dkrow = p.dkbar + ((size_t)t.bh * p.g.Gc + j) * D;
@@ -458,9 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::tma_store_commit();
           // the staging buffers are rewritten only after this read completes:
-          // P/dS by the next tile's first chunk and K by its first chunk load,
-          // both gated on the kv_empty this thread arrives after its delta
+          // P/dS by the next tile's first chunk (after the barrier that
+          // follows its delta) and K by its first chunk load (stage_free)
           ptx::tma_store_wait_read_all();
+          ptx::mbar_arrive(&sm.stage_free);
         }
         ++kc;
       }
