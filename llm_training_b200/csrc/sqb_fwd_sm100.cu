@@ -59,6 +59,7 @@ struct FwdSmem {
   float red[4][2][D];
   uint64_t q_full[NQ], q_empty[NQ];
   uint64_t k_full[NKV], k_empty[NKV], v_full[NKV], v_empty[NKV];
+  uint64_t vbuf_free;  // pooling done with a tile's last V chunk: O may be staged there
   uint64_t s_full[NS], p_full[NS], s_free[NS], o_full, o_free;
   int tile_ring[NQ];
   uint32_t tmem_base;
@@ -107,13 +108,15 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
   if (threadIdx.x == 0) {
     for (int i = 0; i < NQ; ++i) {
       ptx::mbar_init(&sm.q_full[i], 1);
-      ptx::mbar_init(&sm.q_empty[i], 2);   // epilogue store done + pooling done
+      ptx::mbar_init(&sm.q_empty[i], 2);   // last S mma complete + pooling done
     }
     for (int i = 0; i < NKV; ++i) {
       ptx::mbar_init(&sm.k_full[i], 1);
       ptx::mbar_init(&sm.k_empty[i], 2);  // S mma complete + pooling done
       ptx::mbar_init(&sm.v_full[i], 1);
-      ptx::mbar_init(&sm.v_empty[i], 2);  // PV mma complete + pooling done
+      // PV mma complete + pooling done (for a tile's last chunk, whose
+      // buffer stages O: + the O store's read)
+      ptx::mbar_init(&sm.v_empty[i], 2);
     }
     for (int i = 0; i < NS; ++i) {
       ptx::mbar_init(&sm.s_full[i], 1);
@@ -122,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     }
     ptx::mbar_init(&sm.o_full, 1);
     ptx::mbar_init(&sm.o_free, 4);
+    ptx::mbar_init(&sm.vbuf_free, 1);
     ptx::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -276,6 +280,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
                         kk > 0 ? 1u : 0u);
           ptx::mma_commit(&sm.s_full[x]);
           ptx::mma_commit(&sm.k_empty[st]);
+          // Q is read by no later MMA of this tile: the next tile may load
+          if (c == nch - 1) ptx::mma_commit(&sm.q_empty[slot]);
           if (kOverlap && c >= 1) issue_pv(c - 1);
         }
         issue_pv(nch - 1);
@@ -429,11 +435,16 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&sm.p_full[x]);
       }
-      // ---- epilogue: O / l -> bf16 -> swizzled smem (the Q slot) -> TMA store
+      // ---- epilogue: O / l -> bf16 -> swizzled smem -> TMA store.  O is
+      // staged in the V buffer of the tile's last chunk: its last reader, PV,
+      // has completed (o_full) and pooling has finished with it (vbuf_free),
+      // while the Q slot is already taken by the next tile.
       ptx::mbar_wait(&sm.o_full, tc & 1, status, 0x33000000u);
       ptx::tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      uint8_t* stage = sm.q[slot];
+      const int vst = (gc + nch - 1) % NKV;
+      uint8_t* stage = sm.v[vst];
+      ptx::mbar_wait(&sm.vbuf_free, tc & 1, status, 0x34000000u);
       auto emit = [&](const uint32_t (&r)[32], int pc) {
 #pragma unroll
         for (int j8 = 0; j8 < 4; ++j8) {
@@ -469,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
           ptx::tma_store_4d(&tm_o, stage + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
         ptx::tma_store_commit();
         ptx::tma_store_wait_read_all();
-        ptx::mbar_arrive(&sm.q_empty[slot]);
+        ptx::mbar_arrive(&sm.v_empty[vst]);
       }
       gc += nch;
       ++tc;
@@ -527,7 +538,9 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
             ptx::named_barrier(2, 128);
           }
           ptx::named_barrier(2, 128);
-          if (ptid == 0) ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st] : &sm.v_empty[st]);
+          if (ptid == 0)
+            ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st]
+                                     : (t.nsc == 0 ? &sm.vbuf_free : &sm.v_empty[st]));
         }
         // The barrier above orders every pooling thread's summary writes
         // before this release store, which makes them visible to any CTA that
@@ -541,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
           ptx::mbar_wait(&sm.k_full[st], (kc / NKV) & 1, status, 0x42000000u | st);
           ptx::mbar_arrive(&sm.k_empty[st]);
           ptx::mbar_wait(&sm.v_full[st], (kc / NKV) & 1, status, 0x44000000u | st);
-          ptx::mbar_arrive(&sm.v_empty[st]);
+          ptx::mbar_arrive(c == t.nsc - 1 ? &sm.vbuf_free : &sm.v_empty[st]);
         }
         ++kc;
       }
