@@ -328,21 +328,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool any_col = vhi > vlo;
         const int wlo = __reduce_min_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
         const int whi = __reduce_max_sync(0xffffffffu, any_col ? vhi : 0);
-        ptx::mbar_wait(&sm.s_full, kc & 1, status, 0x71000000u);
-        ptx::tc_fence_after();
-#pragma unroll 1
-        for (int pi = 0; pi < 4; ++pi) {
-          const int c0 = (half * 4 + pi) * 16;  // first of this piece's 16 key columns
-          uint32_t sv[16], dp[16];
-          // warp-uniform: the piece holds a column some row of this warp sees
-          const bool live = c0 < N && c0 < whi && c0 + 16 > wlo;
-          if (live) {
-            ptx::tmem_ld16(tmem + lane_off + kColS + c0, sv);
-            ptx::tmem_ld16(tmem + lane_off + kColDP + c0, dp);
-            ptx::tmem_wait_ld();
-            ptx::reg_fence(sv);
-            ptx::reg_fence(dp);
+        // pieces every lane of the warp sees whole need no mask
+        const int lo_max = __reduce_max_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
+        const int hi_min = __reduce_min_sync(0xffffffffu, any_col ? vhi : 0);
+        const float delta_s = delta * p.scale;
+        // this half's four 16-column pieces; a piece is live (warp-uniform)
+        // when it holds a column some row of this warp sees
+        auto col0 = [&](int pi) { return (half * 4 + pi) * 16; };
+        auto live = [&](int pi) {
+          const int c0 = col0(pi);
+          return c0 < N && c0 < whi && c0 + 16 > wlo;
+        };
+        auto load = [&](int pi, uint32_t (&sv)[16], uint32_t (&dp)[16]) {
+          if (live(pi)) {
+            ptx::tmem_ld16(tmem + lane_off + kColS + col0(pi), sv);
+            ptx::tmem_ld16(tmem + lane_off + kColDP + col0(pi), dp);
           }
+        };
+        // P = exp2(S*c - L), dS = P * (dP*scale - delta*scale); masked -> 0
+        auto emit = [&](int pi, const uint32_t (&sv)[16], const uint32_t (&dp)[16]) {
+          const int c0 = col0(pi);
+          const bool lv = live(pi);
+          const bool whole = lv && c0 >= lo_max && c0 + 16 <= hi_min;
 #pragma unroll
           for (int j8 = 0; j8 < 2; ++j8) {
             uint32_t pw[4], dw[4];
@@ -352,11 +359,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
                 const int j = j8 * 8 + h2 * 2 + e;
-                const bool ok = live && (uint32_t)(c0 + j - vlo) < (uint32_t)(vhi - vlo);
-                const float pr = ok ? ptx::ex2(fmaf(__uint_as_float(sv[j]), p.scale_log2, -L))
-                                    : 0.f;
-                pv[e] = pr;
-                dv[e] = ok ? pr * (__uint_as_float(dp[j]) - delta) * p.scale : 0.f;
+                const float pr = ptx::ex2(fmaf(__uint_as_float(sv[j]), p.scale_log2, -L));
+                const float dr = pr * fmaf(__uint_as_float(dp[j]), p.scale, -delta_s);
+                if (whole) {
+                  pv[e] = pr;
+                  dv[e] = dr;
+                } else {
+                  const bool ok = lv && (uint32_t)(c0 + j - vlo) < (uint32_t)(vhi - vlo);
+                  pv[e] = ok ? pr : 0.f;
+                  dv[e] = ok ? dr : 0.f;
+                }
               }
               pw[h2] = ptx::pack_bf16x2(pv[0], pv[1]);
               dw[h2] = ptx::pack_bf16x2(dv[0], dv[1]);
@@ -365,6 +377,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4*>(sm.p + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
             *reinterpret_cast<uint4*>(sm.ds + off) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
           }
+        };
+        ptx::mbar_wait(&sm.s_full, kc & 1, status, 0x71000000u);
+        ptx::tc_fence_after();
+#pragma unroll 1
+        for (int pi = 0; pi < 4; ++pi) {
+          uint32_t sv[16], dp[16];
+          load(pi, sv, dp);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence(sv);
+          ptx::reg_fence(dp);
+          emit(pi, sv, dp);
         }
         ptx::fence_proxy_async_smem();
         ptx::tc_fence_before();
