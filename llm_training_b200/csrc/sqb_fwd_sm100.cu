@@ -334,9 +334,9 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         const int q_lo = whi > wlo ? (wlo >> 4) : 0;
         const int q_hi = whi > wlo ? min((whi + 15) >> 4, nq) : 0;
         const uint32_t vspan = any_col ? (uint32_t)(vhi - vlo) : 0u;
-        // Both passes walk the live pieces with two 16-column buffers, issuing
-        // the next piece's TMEM load before this piece's math.
-        uint32_t bufA[16], bufB[16];
+        // Both passes walk the live pieces two at a time with one 32-column
+        // TMEM load (fewer load round trips than 16-column double buffering;
+        // an odd last pair reads 16 columns past the live range, unused).
         // pass 1: row max over the visible columns (masked -> -inf)
         float mx = -INFINITY;
         {
@@ -351,19 +351,13 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
             }
             mx = fmaxf(mx, fmaxf(m0, m1));
           };
-          if (q_lo < q_hi) ptx::tmem_ld16(s_addr + q_lo * 16, bufA);
           for (int q = q_lo; q < q_hi; q += 2) {
+            uint32_t r[32];
+            ptx::tmem_ld32(s_addr + q * 16, r);
             ptx::tmem_wait_ld();
-            ptx::reg_fence(bufA);
-            const bool b = q + 1 < q_hi;
-            if (b) ptx::tmem_ld16(s_addr + q * 16 + 16, bufB);
-            maxp(bufA, q);
-            if (b) {
-              ptx::tmem_wait_ld();
-              ptx::reg_fence(bufB);
-              if (q + 2 < q_hi) ptx::tmem_ld16(s_addr + q * 16 + 32, bufA);
-              maxp(bufB, q + 1);
-            }
+            ptx::reg_fence(r);
+            maxp(*reinterpret_cast<const uint32_t(*)[16]>(r), q);
+            if (q + 1 < q_hi) maxp(*reinterpret_cast<const uint32_t(*)[16]>(r + 16), q + 1);
           }
         }
         const float m_new = fmaxf(m, mx * p.scale_log2);
@@ -413,19 +407,13 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
           // live range can be zeroed first (their P columns are below every
           // live S column); those above only after the live pieces are read
           for (int q = 0; q < q_lo; ++q) ptx::tmem_st8(s_addr + q * 8, zero8);
-          if (q_lo < q_hi) ptx::tmem_ld16(s_addr + q_lo * 16, bufA);
           for (int q = q_lo; q < q_hi; q += 2) {
+            uint32_t r[32];
+            ptx::tmem_ld32(s_addr + q * 16, r);
             ptx::tmem_wait_ld();
-            ptx::reg_fence(bufA);
-            const bool b = q + 1 < q_hi;
-            if (b) ptx::tmem_ld16(s_addr + q * 16 + 16, bufB);
-            expp(bufA, q);
-            if (b) {
-              ptx::tmem_wait_ld();
-              ptx::reg_fence(bufB);
-              if (q + 2 < q_hi) ptx::tmem_ld16(s_addr + q * 16 + 32, bufA);
-              expp(bufB, q + 1);
-            }
+            ptx::reg_fence(r);
+            expp(*reinterpret_cast<const uint32_t(*)[16]>(r), q);
+            if (q + 1 < q_hi) expp(*reinterpret_cast<const uint32_t(*)[16]>(r + 16), q + 1);
           }
           for (int q = q_hi; q < nq; ++q) ptx::tmem_st8(s_addr + q * 8, zero8);
           l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
