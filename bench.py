@@ -1,6 +1,8 @@
 """Benchmark: sqrt-block attention forward+backward at B=1, H=16, T=16384, D=128, bf16.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload attn-t4k|attn-t8k|attn-t16k|attn-t32k|attn-t64k|gpt2-small|
+                                gpt2-medium-8k]
 
 One step = one forward (sqb_fwd) and one backward (sqb_bwd) of the attention
 operator over the whole workload.  ``value`` is whole-job algorithmic HBM
@@ -37,6 +39,10 @@ if REPO not in sys.path:
 METRIC = "sqrt-block attn fwd+bwd ms & HBM GB/s at T=16K; GPT-2 small train tokens/sec"
 B, H, T, D = 1, 16, 16384, 128
 ELT = 2  # bf16
+# the long-context sweep (B=1, H=16, D=128, default block length); attn-t16k is
+# the headline point and the default
+SWEEP = {"attn-t4k": 4096, "attn-t8k": 8192, "attn-t16k": 16384, "attn-t32k": 32768,
+         "attn-t64k": 65536}
 
 
 def algorithmic_bytes(B_, H_, T_, D_, elt=ELT, fwd=True, bwd=True):
@@ -174,6 +180,8 @@ def run_reference(args, world, rank):
     """CPU restatement of the operator, timed on the host cores."""
     if rank != 0:
         return
+    from oracle.sqrtblock_oracle import default_block
+
     heads = 1
     sample_bytes = algorithmic_bytes(B, heads, T, D)
     cpu_sample_time(heads, 1)  # warm-up allocations and thread pool
@@ -191,8 +199,9 @@ def run_reference(args, world, rank):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(full_ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
-        "config": {"workload": "sqrt-block attention fwd+bwd", "B": B, "H": H, "T": T, "D": D,
-                   "block": 128, "parallelism": f"heads x {world} ranks (rank 0 timed)"},
+        "config": {"workload": f"sqrt-block attention fwd+bwd (sweep point T={T})", "B": B,
+                   "H": H, "T": T, "D": D, "block": default_block(T),
+                   "parallelism": f"heads x {world} ranks (rank 0 timed)"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{heads} of {H} heads per step, fp32 torch, "
                                    "ms_per_step scaled to all heads"},
@@ -210,7 +219,7 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     host = make_inputs(args.seed, rank, dev)
     q, k, v, do = [x.to(dev) for x in host]
-    block = 128
+    block = _lib.geometry(T)[0]  # the default block length of this T
     fwd_impl = bwd_impl = args.kernels
     if args.kernels == "auto":
         # the tcgen05 family where it has a kernel for this shape, else SIMT
@@ -232,6 +241,13 @@ def run_ours(args, world, rank, local):
     impl = f"fwd:{fwd_impl},bwd:{bwd_impl}"
 
     stream = torch.cuda.current_stream(dev)
+    # Q, K, V, dO and O resident: above 2x the 126 MB L2 nothing survives from
+    # one step to the next; below it (T <= 8192 here) L2 is flushed between
+    # timed steps (a 512 MB write) and a step is timed from the forward's start
+    # to the backward's end, so the flush is not counted.
+    resident = 5 * B * H * T * D * ELT
+    flush = resident < 2 * 126 * 2**20
+    flush_buf = torch.empty(512 * 2**20, dtype=torch.uint8, device=dev) if flush else None
     f_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
     b_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
 
@@ -263,6 +279,8 @@ def run_ours(args, world, rank, local):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for i in range(args.steps):
+            if flush:
+                flush_buf.zero_()
             step(i)
         end.record(stream)
         torch.cuda.synchronize()
@@ -272,7 +290,12 @@ def run_ours(args, world, rank, local):
     fwd_ms = statistics.mean(f_ev[2 * i].elapsed_time(f_ev[2 * i + 1]) for i in range(args.steps))
     bwd_ms = statistics.mean(b_ev[2 * i].elapsed_time(b_ev[2 * i + 1]) for i in range(args.steps))
 
-    ms_per_step = total_ms / args.steps
+    if flush:
+        step_ms = statistics.mean(f_ev[2 * i].elapsed_time(b_ev[2 * i + 1])
+                                  for i in range(args.steps))
+        ms_per_step = max_over_ranks(step_ms, world)
+    else:
+        ms_per_step = total_ms / args.steps
     step_bytes = algorithmic_bytes(B, H, T, D)
     value = step_bytes * world / (ms_per_step * 1e-3) / 1e9
 
@@ -317,7 +340,7 @@ def run_ours(args, world, rank, local):
                 "bwd": {"ms": round(bwd_ms, 4),
                         "GBps": round(bwd_bytes / (bwd_ms * 1e-3) / 1e9, 1)}}
     traffic_path = os.path.join(REPO, "profiles", "dram_traffic.json")
-    if os.path.exists(traffic_path):
+    if T == 16384 and os.path.exists(traffic_path):  # captured at T=16384
         try:
             roofline["traffic"] = json.load(open(traffic_path)).get(dom[0])
         except Exception:
@@ -337,10 +360,13 @@ def run_ours(args, world, rank, local):
             "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded per rank",
-            "config": {"workload": "sqrt-block attention fwd+bwd (sweep point T=16384)",
+            "config": {"workload": f"sqrt-block attention fwd+bwd (sweep point T={T})",
                        "B": B, "H_per_rank": H, "T": T, "D": D, "block": block,
                        "parallelism": f"heads x {world} ranks", "kernels": impl,
-                       "l2": "inputs 4 x 67 MB > 126 MB L2; no flush"},
+                       "l2": (f"L2 flushed between steps (512 MB write, not timed); resident "
+                              f"Q/K/V/dO/O {resident / 2**20:.0f} MB" if flush else
+                              f"resident Q/K/V/dO/O {resident / 2**20:.0f} MB > 2 x 126 MB L2; "
+                              "no flush")},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(step_bytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -431,13 +457,16 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--warmup-seconds", type=float, default=0.5,
                     help="keep warming up at least this long (clock sampler needs samples)")
-    ap.add_argument("--workload", choices=["attn-t16k"] + sorted(TRAIN_WORKLOADS),
+    ap.add_argument("--workload", choices=sorted(SWEEP) + sorted(TRAIN_WORKLOADS),
                     default="attn-t16k",
-                    help="attn-t16k: the attention op (default); gpt2-*: a training step")
+                    help="attn-t*: the attention op at that sweep length (attn-t16k is the "
+                         "default); gpt2-*: a training step")
     args = ap.parse_args()
+    global T
+    T = SWEEP.get(args.workload, T)
     world, rank, local = init_dist()
     try:
-        if args.workload != "attn-t16k":
+        if args.workload not in SWEEP:
             if args.impl == "reference":
                 if rank == 0:
                     print(json.dumps({"impl": "reference", "unavailable":

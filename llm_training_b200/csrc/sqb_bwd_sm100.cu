@@ -47,9 +47,17 @@ struct BwdParams {
   int64_t o_sb, o_st, o_sh;
   float* dkbar;  // fp32 (BH, Gc, D) accumulators, zero between launches
   float* dvbar;
+  // b > 128: fp32 (BH, G, xrows, D) accumulators of the dK / dV that a block's
+  // later sub-tiles contribute to the keys of its earlier ones (xrows =
+  // (sub-tiles per block - 1) * 128), zero between launches
+  float* dkx;
+  float* dvx;
+  uint32_t* readers;  // b > 128: per (batch*head, block) count of sub-tiles that read its sums
+  int G, xrows;
   uint32_t* ctrl;
   uint32_t* flags;
   int flags_stride;
+  int store_rows;  // rows per dQ/dK/dV store box
 };
 
 template <int D>
@@ -79,7 +87,7 @@ constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-template <int D>
+template <int D, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -134,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
   auto tile_of = [&](int n) {
-    return make_tile(p.g, p.H, NT - 1 - n / p.BH, n % p.BH);
+    return make_tile<kSplit>(p.g, p.H, NT - 1 - n / p.BH, n % p.BH);
   };
 
   if (warp == 0) {
@@ -177,7 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // load also waits for the previous tile's dQ staging in the K buffer
         // to be read by its TMA store; its first V load waits for delta,
         // which reads O from the V buffer.
-        for (int c = 0; c <= t.nsc; ++c) {
+        const int nch = t.nsc + t.nin;  // summary chunks, then in-block chunks
+        for (int c = 0; c < nch; ++c) {
           auto load_k = [&]() {
             ptx::mbar_wait(&sm.k_empty, (kc & 1) ^ 1, status, 0x51000000u);
             if (c == 0 && tc > 0)
@@ -189,10 +198,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int a = 0; a < kAtoms; ++a)
                 ptx::tma_load_3d(sm.k + a * kAtomBytes, &tm_kbar, &sm.k_full, a * 64, sc.w, t.bh);
             } else {
+              const InChunk ic = in_chunk<kSplit>(t, c - t.nsc);
               ptx::mbar_arrive_expect_tx(&sm.k_full, kAtoms * box_bytes);
 #pragma unroll
               for (int a = 0; a < kAtoms; ++a)
-                ptx::tma_load_4d(sm.k + a * kAtomBytes, &tm_k, &sm.k_full, a * 64, t.h, t.r0,
+                ptx::tma_load_4d(sm.k + a * kAtomBytes, &tm_k, &sm.k_full, a * 64, t.h, ic.k0,
                                  t.n);
             }
           };
@@ -206,10 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int a = 0; a < kAtoms; ++a)
                 ptx::tma_load_3d(sm.v + a * kAtomBytes, &tm_vbar, &sm.v_full, a * 64, sc.w, t.bh);
             } else {
+              const InChunk ic = in_chunk<kSplit>(t, c - t.nsc);
               ptx::mbar_arrive_expect_tx(&sm.v_full, kAtoms * box_bytes);
 #pragma unroll
               for (int a = 0; a < kAtoms; ++a)
-                ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_v, &sm.v_full, a * 64, t.h, t.r0,
+                ptx::tma_load_4d(sm.v + a * kAtomBytes, &tm_v, &sm.v_full, a * 64, t.h, ic.k0,
                                  t.n);
             }
           };
@@ -243,8 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n < 0) break;
         const Tile t = tile_of(n);
         const int kq = round16(t.rows) / 16;  // k-steps over query rows
-        for (int c = 0; c <= t.nsc; ++c) {
-          const int N = c < t.nsc ? sum_chunk(t, c).n16 : t.n_in;
+        const int nch = t.nsc + t.nin;
+        for (int c = 0; c < nch; ++c) {
+          const int N = c < t.nsc ? sum_chunk(t, c).n16 : in_chunk<kSplit>(t, c - t.nsc).n;
           ptx::mbar_wait(&sm.k_full, kc & 1, status, 0x61000000u);
           if (kc > 0) ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
           ptx::tc_fence_after();
@@ -274,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mma_ss(tmem + kColDP, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
                         kk > 0 ? 1u : 0u);
           ptx::mma_commit(&sm.g_full);
-          if (c == t.nsc) ptx::mma_commit(&sm.ld_empty);  // Q, dO, V no longer read
+          if (c == nch - 1) ptx::mma_commit(&sm.ld_empty);  // Q, dO, V no longer read
           ++kc;
         }
         ++tc;
@@ -397,14 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
       };
 
-      // ---- summary chunks: add dKc / dVc to the summary accumulators
-      for (int c = 0; c < t.nsc; ++c) {
-        const SumChunk sc = sum_chunk(t, c);
-        softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
-        const int j = sc.w + row;  // this lane's summary
-        const bool ok = row >= sc.lo - sc.w && row < sc.e - sc.w;
-        float* dkrow = p.dkbar + ((size_t)t.bh * p.g.Gc + j) * D;
-        float* dvrow = p.dvbar + ((size_t)t.bh * p.g.Gc + j) * D;
+      // Adds this lane's row of a chunk's dKc / dVc (TMEM, S and dP columns,
+      // this warp's column half) to fp32 rows of the workspace with vector
+      // atomics, then frees the columns for the next chunk's S/dP.
+      auto drain = [&](float* dkrow, float* dvrow, bool ok) {
 #pragma unroll 1
         for (int pc = 0; pc < kHalfD / 16; ++pc) {
           const int col0 = half * kHalfD + pc * 16;
@@ -430,19 +438,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&sm.g_free);
         ++kc;
+      };
+
+      // ---- summary chunks: add dKc / dVc to the summary accumulators
+      for (int c = 0; c < t.nsc; ++c) {
+        const SumChunk sc = sum_chunk(t, c);
+        softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
+        const int j = sc.w + row;  // this lane's summary
+        const size_t jr = (size_t)t.bh * p.g.Gc + j;
+        drain(p.dkbar + jr * D, p.dvbar + jr * D, row >= sc.lo - sc.w && row < sc.e - sc.w);
+      }
+
+      // ---- b > 128: in-block chunks before this sub-tile's rows.  Every key is
+      // visible to every row; their dKc / dVc belong to the keys of earlier
+      // sub-tiles of the block and are added to the workspace accumulators
+      // that those sub-tiles' epilogues read.
+      for (int u = 0; u + 1 < t.nin; ++u) {
+        softmax_grad(kTileRows, 0, valid ? kTileRows : 0);
+        const size_t xr = ((size_t)t.bh * p.G + t.blk0) * p.xrows + u * kTileRows + row;
+        drain(p.dkx + xr * D, p.dvx + xr * D, true);
       }
 
       // ---- publish (by the publisher warp): this warp's additions are done
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&sm.red_done);
 
-      // ---- in-block chunk
-      softmax_grad(t.n_in, valid ? blk_t * p.g.b - t.r0 : 0, valid ? row + 1 : 0);
+      // ---- the in-block chunk of the tile's own rows (causal)
+      softmax_grad(t.n_in, valid ? max(0, blk_t * p.g.b - t.r0) : 0, valid ? row + 1 : 0);
       // the publisher has staged sum / b of the tile's complete blocks
       ptx::mbar_wait(&sm.sums_ready, tc & 1, status, 0x73000000u);
       {
         const bool complete = valid && blk_t < p.g.Gc;  // this lane's key is in a full block
         const int lb_t = valid ? blk_t - t.blk0 : 0;
+        // b > 128: a sub-tile followed by others in its block adds their
+        // contributions to its keys (and re-zeroes them)
+        const bool cross = kSplit && valid && t.sub + 1 < block_tiles(p.g, t.blk0);
+        const size_t xr = ((size_t)t.bh * p.G + t.blk0) * p.xrows + t.sub * kTileRows + row;
         const float* skrow = sm.sgrad[0][lb_t];
         const float* svrow = sm.sgrad[1][lb_t];
 #pragma unroll 1
@@ -468,6 +499,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float4 k1 = *reinterpret_cast<const float4*>(skrow + col + 4);
               const float4 v0 = *reinterpret_cast<const float4*>(svrow + col);
               const float4 v1 = *reinterpret_cast<const float4*>(svrow + col + 4);
+              fk[0] += k0.x; fk[1] += k0.y; fk[2] += k0.z; fk[3] += k0.w;
+              fk[4] += k1.x; fk[5] += k1.y; fk[6] += k1.z; fk[7] += k1.w;
+              fv[0] += v0.x; fv[1] += v0.y; fv[2] += v0.z; fv[3] += v0.w;
+              fv[4] += v1.x; fv[5] += v1.y; fv[6] += v1.z; fv[7] += v1.w;
+            }
+            if (cross) {
+              float4* xk = reinterpret_cast<float4*>(p.dkx + xr * D + col);
+              float4* xv = reinterpret_cast<float4*>(p.dvx + xr * D + col);
+              const float4 k0 = __ldcg(xk), k1 = __ldcg(xk + 1);
+              const float4 v0 = __ldcg(xv), v1 = __ldcg(xv + 1);
+              const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+              __stcg(xk, z);
+              __stcg(xk + 1, z);
+              __stcg(xv, z);
+              __stcg(xv + 1, z);
               fk[0] += k0.x; fk[1] += k0.y; fk[2] += k0.z; fk[3] += k0.w;
               fk[4] += k1.x; fk[5] += k1.y; fk[6] += k1.z; fk[7] += k1.w;
               fv[0] += v0.x; fv[1] += v0.y; fv[2] += v0.z; fv[3] += v0.w;
@@ -511,9 +557,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (gtid == 0) {
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a) {
-            ptx::tma_store_4d(&tm_dk, sm.p + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
-            ptx::tma_store_4d(&tm_dv, sm.ds + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
-            ptx::tma_store_4d(&tm_dq, sm.k + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+            for (int r = 0; r < t.rows; r += p.store_rows) {
+              const uint32_t off = a * kAtomBytes + r * 128;
+              ptx::tma_store_4d(&tm_dk, sm.p + off, a * 64, t.h, t.r0 + r, t.n);
+              ptx::tma_store_4d(&tm_dv, sm.ds + off, a * 64, t.h, t.r0 + r, t.n);
+              ptx::tma_store_4d(&tm_dq, sm.k + off, a * 64, t.h, t.r0 + r, t.n);
+            }
           }
           ptx::tma_store_commit();
           // the staging buffers are rewritten only after this read completes:
@@ -552,7 +601,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::counters_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT, token,
                                status, (uint32_t)n);
       if (tc > 0) ptx::mbar_wait(&sm.sgrad_free, (tc - 1) & 1, status, 0x82000000u);
-      const int nfull = max(0, min(p.g.R / p.g.b, p.g.Gc - t.blk0));
+      constexpr bool split = kSplit;
+      const int nb = split ? 1 : p.g.R / p.g.b;  // blocks the tile's rows cover
+      const int nfull = max(0, min(nb, p.g.Gc - t.blk0));
       for (int lb = 0; lb < nfull; ++lb) {
         const size_t base = ((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D;
         for (int i = lane * 4; i < D; i += 128) {
@@ -562,8 +613,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_float4(k4.x * inv_b, k4.y * inv_b, k4.z * inv_b, k4.w * inv_b);
           *reinterpret_cast<float4*>(&sm.sgrad[1][lb][i]) =
               make_float4(v4.x * inv_b, v4.y * inv_b, v4.z * inv_b, v4.w * inv_b);
-          *reinterpret_cast<float4*>(p.dkbar + base + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4*>(p.dvbar + base + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        // The sums are re-zeroed by their last reader: the tile itself for
+        // b <= 128; for b > 128, of the block's sub-tiles (which read in any
+        // order), the one whose count increment (acq_rel, after its reads)
+        // completes the count.
+        bool last = true;
+        if (split) {
+          __syncwarp();
+          uint32_t prev = 0;
+          if (lane == 0)
+            prev = ptx::atom_add_acq_rel_gpu(p.readers + (size_t)t.bh * p.G + t.blk0, 1u);
+          prev = __shfl_sync(0xffffffffu, prev, 0);
+          last = prev + 1 == (uint32_t)p.g.tpb;
+          if (last && lane == 0) p.readers[(size_t)t.bh * p.G + t.blk0] = 0u;
+          __syncwarp();
+        }
+        if (last) {
+          for (int i = lane * 4; i < D; i += 128) {
+            *reinterpret_cast<float4*>(p.dkbar + base + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(p.dvbar + base + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
       }
       __syncwarp();
@@ -590,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D>
+template <int D, bool kSplit>
 int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
            uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   BwdParams p;
@@ -598,7 +668,11 @@ int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorV
   p.g.b = pr.b;
   p.g.Gc = pr.Gc;
   p.g.R = tile_rows(pr.b);
-  p.g.tiles_per_seq = (pr.T + p.g.R - 1) / p.g.R;
+  p.g.tiles_per_seq = tiles_per_seq(pr.T, pr.b);
+  p.g.tpb = tiles_per_block(pr.b);
+  p.store_rows = store_rows(pr.b);
+  p.G = pr.G;
+  p.xrows = pr.b > 128 ? (tiles_per_block(pr.b) - 1) * 128 : 0;
   p.H = pr.H;
   p.BH = pr.B * pr.H;
   p.total_tiles = p.g.tiles_per_seq * p.BH;
@@ -611,15 +685,18 @@ int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorV
   p.o_sh = o.sh;
   p.dkbar = reinterpret_cast<float*>(ws + wl.dkbar);
   p.dvbar = reinterpret_cast<float*>(ws + wl.dvbar);
+  p.dkx = reinterpret_cast<float*>(ws + wl.dkx);
+  p.dvx = reinterpret_cast<float*>(ws + wl.dvx);
+  p.readers = reinterpret_cast<uint32_t*>(ws + wl.readers);
   p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_bwd);
   p.flags_stride = wl.tiles_per_seq;
   const size_t smem = sizeof(BwdSmem<D>) + 1024;
-  if (cudaFuncSetAttribute(bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(bwd_kernel<D, kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
     return SQB_ERR_LAUNCH;
   const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
-  bwd_kernel<D><<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.dout, tm.dq, tm.dk,
+  bwd_kernel<D, kSplit><<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.dout, tm.dq, tm.dk,
                                                    tm.dv, tm.kbar, tm.vbar, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
@@ -628,8 +705,13 @@ int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorV
 
 int launch_backward(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
                     uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
-  if (pr.D == 64) return launch<64>(pr, tm, lse, o, ws, wl, num_sms, stream);
-  if (pr.D == 128) return launch<128>(pr, tm, lse, o, ws, wl, num_sms, stream);
+  const bool split = pr.b > 128;
+  if (pr.D == 64)
+    return split ? launch<64, true>(pr, tm, lse, o, ws, wl, num_sms, stream)
+                 : launch<64, false>(pr, tm, lse, o, ws, wl, num_sms, stream);
+  if (pr.D == 128)
+    return split ? launch<128, true>(pr, tm, lse, o, ws, wl, num_sms, stream)
+                 : launch<128, false>(pr, tm, lse, o, ws, wl, num_sms, stream);
   return SQB_ERR_UNSUPPORTED;
 }
 

@@ -44,6 +44,7 @@ struct FwdParams {
   uint32_t* ctrl;
   uint32_t* flags;
   int flags_stride;
+  int store_rows;  // rows per O store box
 };
 
 // Pipeline depths: NQ query-tile slots, NKV key/value chunk stages, NS score
@@ -88,7 +89,7 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 q) {
   }
 }
 
-template <int D, int NQ, int NKV, int NS>
+template <int D, int NQ, int NKV, int NS, bool kSplit>
 __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         if (n < 0) ptx::mbar_arrive(&sm.q_full[slot]);
       }
       if (n < 0) break;
-      const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
+      const Tile t = make_tile<kSplit>(p.g, p.H, n / p.BH, n % p.BH);
       if (lane == 0) {
         ptx::mbar_arrive_expect_tx(&sm.q_full[slot], kAtoms * box_bytes);
 #pragma unroll
@@ -178,7 +179,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
           ptx::tma_load_4d(sm.q[slot] + a * kAtomBytes, &tm_q, &sm.q_full[slot], a * 64, t.h,
                            t.r0, t.n);
       }
-      {
+      for (int u = 0; u < t.nin; ++u) {
+        const InChunk ic = in_chunk<kSplit>(t, u);
         const int st = kc % NKV;
         const uint32_t par = ((kc / NKV) & 1) ^ 1;
         ptx::mbar_wait(&sm.k_empty[st], par, status, 0x11000000u | st);
@@ -187,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a)
             ptx::tma_load_4d(sm.k[st] + a * kAtomBytes, &tm_k, &sm.k_full[st], a * 64, t.h,
-                             t.r0, t.n);
+                             ic.k0, t.n);
         }
         ptx::mbar_wait(&sm.v_empty[st], par, status, 0x13000000u | st);
         if (lane == 0) {
@@ -195,13 +197,13 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a)
             ptx::tma_load_4d(sm.v[st] + a * kAtomBytes, &tm_v, &sm.v_full[st], a * 64, t.h,
-                             t.r0, t.n);
+                             ic.k0, t.n);
         }
         ++kc;
       }
       if (t.nsc > 0) {
         // every tile holding one of the needed summaries has published
-        const int s_need = ((t.ns - 1) * p.g.b) / p.g.R;
+        const int s_need = summary_tile<kSplit>(p.g, t.ns - 1);
         ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, 0, s_need + 1, token,
                               status, (uint32_t)n);
         if (lane == 0) ptx::fence_proxy_async_global();
@@ -241,10 +243,12 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         ptx::mbar_wait(&sm.q_full[slot], (tc / NQ) & 1, status, 0x20000000u | slot);
         const int n = sm.tile_ring[slot];
         if (n < 0) break;
-        const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
-        const int nch = 1 + t.nsc;
+        const Tile t = make_tile<kSplit>(p.g, p.H, n / p.BH, n % p.BH);
+        const int nch = t.nin + t.nsc;
         const uint32_t q_saddr = ptx::smem_u32(sm.q[slot]);
-        auto chunk_n = [&](int c) { return c == 0 ? t.n_in : sum_chunk(t, c - 1).n16; };
+        auto chunk_n = [&](int c) {
+          return c < t.nin ? in_chunk<kSplit>(t, c).n : sum_chunk(t, c - t.nin).n16;
+        };
         auto issue_pv = [&](int c) {
           const int g = gc + c, x = g % NS, st = (kc + c) % NKV;
           ptx::mbar_wait(&sm.p_full[x], (g / NS) & 1, status, 0x21000000u | x);
@@ -302,8 +306,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       ptx::mbar_wait(&sm.q_full[slot], (tc / NQ) & 1, status, 0x30000000u | slot);
       const int n = sm.tile_ring[slot];
       if (n < 0) break;
-      const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
-      const int nch = 1 + t.nsc;
+      const Tile t = make_tile<kSplit>(p.g, p.H, n / p.BH, n % p.BH);
+      const int nch = t.nin + t.nsc;
       const int tq = t.r0 + row;
       const bool valid = row < t.rows;
       const int blk_t = valid ? tq / p.g.b : 0;
@@ -312,12 +316,14 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       for (int c = 0; c < nch; ++c) {
         const int g = gc + c, x = g % NS;
         int N, vlo, vhi;  // MMA width and the valid column range [vlo, vhi)
-        if (c == 0) {
-          N = t.n_in;
-          vlo = valid ? blk_t * p.g.b - t.r0 : 0;
-          vhi = valid ? row + 1 : 0;
+        if (c < t.nin) {
+          // in-block keys [k0, k0 + N): those of the row's block up to the row
+          const InChunk ic = in_chunk<kSplit>(t, c);
+          N = ic.n;
+          vlo = valid ? max(0, blk_t * p.g.b - ic.k0) : 0;
+          vhi = valid ? min(tq - ic.k0 + 1, N) : 0;
         } else {
-          const SumChunk sc = sum_chunk(t, c - 1);
+          const SumChunk sc = sum_chunk(t, c - t.nin);
           N = sc.n16;
           vlo = sc.lo - sc.w;
           vhi = min(sc.e, lim) - sc.w;
@@ -465,7 +471,9 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       if (warp == 2 && lane == 0) {
 #pragma unroll
         for (int a = 0; a < kAtoms; ++a)
-          ptx::tma_store_4d(&tm_o, stage + a * kAtomBytes, a * 64, t.h, t.r0, t.n);
+          for (int r = 0; r < t.rows; r += p.store_rows)
+            ptx::tma_store_4d(&tm_o, stage + a * kAtomBytes + r * 128, a * 64, t.h, t.r0 + r,
+                              t.n);
         ptx::tma_store_commit();
         ptx::tma_store_wait_read_all();
         ptx::mbar_arrive(&sm.v_empty[vst]);
@@ -487,54 +495,103 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       ptx::mbar_wait(&sm.q_full[slot], (tc / NQ) & 1, status, 0x40000000u | slot);
       const int n = sm.tile_ring[slot];
       if (n < 0) break;
-      const Tile t = make_tile(p.g, p.H, n / p.BH, n % p.BH);
+      const Tile t = make_tile<kSplit>(p.g, p.H, n / p.BH, n % p.BH);
       {
-        const int st = kc % NKV;
-        const int nb = p.g.R / p.g.b;
+        // b <= 128: each complete block of the tile's single in-block chunk is
+        // pooled and written on its own.  b > 128: the last sub-tile of a
+        // complete block sees the whole block in its in-block chunks and
+        // accumulates it across them; the other sub-tiles only pass the
+        // chunks through.
+        constexpr bool split = kSplit;
+        const bool pool_split = split && t.blk0 < p.g.Gc && t.sub == p.g.tpb - 1;
+        const int nb = split ? 0 : p.g.R / p.g.b;
         const int nfull = max(0, min(nb, p.g.Gc - t.blk0));
-        // K then V: each buffer is released as soon as its own sums are read,
-        // so the summary chunk's Kbar load can start while V is still pooled.
-#pragma unroll 1
-        for (int kv = 0; kv < 2; ++kv) {
-          ptx::mbar_wait(kv == 0 ? &sm.k_full[st] : &sm.v_full[st], (kc / NKV) & 1, status,
-                         (kv == 0 ? 0x41000000u : 0x43000000u) | st);
-          const uint8_t* buf = kv == 0 ? sm.k[st] : sm.v[st];
-          __nv_bfloat16* dst = kv == 0 ? p.kbar : p.vbar;
-          for (int lb = 0; lb < nfull; ++lb) {
-            float a[8];
+        float acck[8], accv[8];  // b > 128: this thread's column sums of K, V
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] = 0.f;
-            if (cc < D / 8) {
-              for (int i = 0; i < p.g.b / 8; ++i) {
-                const int r = lb * p.g.b + rg + 8 * i;
-                add_bf16x8(a, *reinterpret_cast<const uint4*>(buf + swz_offset(r, cc * 8)));
+        for (int j = 0; j < 8; ++j) acck[j] = accv[j] = 0.f;
+        for (int u = 0; u < t.nin; ++u) {
+          const int st = kc % NKV;
+          const int urows = u == t.nin - 1 ? t.rows : kTileRows;
+          // the tile's last chunk: its V buffer stages O (see the epilogue)
+          const bool last = u == t.nin - 1 && t.nsc == 0;
+          // K then V: each buffer is released as soon as its own sums are read,
+          // so the next chunk's K load can start while V is still pooled.
+#pragma unroll 1
+          for (int kv = 0; kv < 2; ++kv) {
+            ptx::mbar_wait(kv == 0 ? &sm.k_full[st] : &sm.v_full[st], (kc / NKV) & 1, status,
+                           (kv == 0 ? 0x41000000u : 0x43000000u) | st);
+            const uint8_t* buf = kv == 0 ? sm.k[st] : sm.v[st];
+            __nv_bfloat16* dst = kv == 0 ? p.kbar : p.vbar;
+            for (int lb = 0; lb < nfull; ++lb) {
+              float a[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a[j] = 0.f;
+              if (cc < D / 8) {
+                for (int i = 0; i < p.g.b / 8; ++i) {
+                  const int r = lb * p.g.b + rg + 8 * i;
+                  add_bf16x8(a, *reinterpret_cast<const uint4*>(buf + swz_offset(r, cc * 8)));
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], 16);
+              if ((ptid & 16) == 0 && cc < D / 8) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sm.red[pw][kv][cc * 8 + j] = a[j];
+              }
+              ptx::named_barrier(2, 128);
+              if (ptid < D) {
+                const float sum = sm.red[0][kv][ptid] + sm.red[1][kv][ptid] +
+                                  sm.red[2][kv][ptid] + sm.red[3][kv][ptid];
+                dst[((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D + ptid] =
+                    __float2bfloat16_rn(sum * inv_b);
+              }
+              ptx::named_barrier(2, 128);
+            }
+            if (pool_split && cc < D / 8) {
+              for (int i = 0; i < urows / 8; ++i) {
+                const uint4 w = *reinterpret_cast<const uint4*>(buf + swz_offset(rg + 8 * i, cc * 8));
+                if (kv == 0)
+                  add_bf16x8(acck, w);
+                else
+                  add_bf16x8(accv, w);
               }
             }
+            ptx::named_barrier(2, 128);
+            if (ptid == 0)
+              ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st]
+                                       : (last ? &sm.vbuf_free : &sm.v_empty[st]));
+          }
+          ++kc;
+        }
+        if (pool_split) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], 16);
-            if ((ptid & 16) == 0 && cc < D / 8) {
+          for (int j = 0; j < 8; ++j) {
+            acck[j] += __shfl_xor_sync(0xffffffffu, acck[j], 16);
+            accv[j] += __shfl_xor_sync(0xffffffffu, accv[j], 16);
+          }
+          if ((ptid & 16) == 0 && cc < D / 8) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) sm.red[pw][kv][cc * 8 + j] = a[j];
+            for (int j = 0; j < 8; ++j) {
+              sm.red[pw][0][cc * 8 + j] = acck[j];
+              sm.red[pw][1][cc * 8 + j] = accv[j];
             }
+          }
+#pragma unroll 1
+          for (int kv = 0; kv < 2; ++kv) {
             ptx::named_barrier(2, 128);
             if (ptid < D) {
               const float sum = sm.red[0][kv][ptid] + sm.red[1][kv][ptid] +
                                 sm.red[2][kv][ptid] + sm.red[3][kv][ptid];
-              dst[((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D + ptid] =
+              (kv == 0 ? p.kbar : p.vbar)[((size_t)t.bh * p.g.Gc + t.blk0) * D + ptid] =
                   __float2bfloat16_rn(sum * inv_b);
             }
             ptx::named_barrier(2, 128);
           }
-          ptx::named_barrier(2, 128);
-          if (ptid == 0)
-            ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st]
-                                     : (t.nsc == 0 ? &sm.vbuf_free : &sm.v_empty[st]));
         }
-        // The barrier above orders every pooling thread's summary writes
+        // The barriers above order every pooling thread's summary writes
         // before this release store, which makes them visible to any CTA that
         // acquires the flag.
         if (ptid == 0) ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
-        ++kc;
       }
       for (int c = 0; c < t.nsc; ++c) {
         if (ptid == 0) {
@@ -570,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
   }
 }
 
-template <int D, int NQ, int NKV, int NS>
+template <int D, int NQ, int NKV, int NS, bool kSplit>
 int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
            uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   FwdParams p;
@@ -578,7 +635,9 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
   p.g.b = pr.b;
   p.g.Gc = pr.Gc;
   p.g.R = tile_rows(pr.b);
-  p.g.tiles_per_seq = (pr.T + p.g.R - 1) / p.g.R;
+  p.g.tiles_per_seq = tiles_per_seq(pr.T, pr.b);
+  p.g.tpb = tiles_per_block(pr.b);
+  p.store_rows = store_rows(pr.b);
   p.H = pr.H;
   p.BH = pr.B * pr.H;
   p.total_tiles = p.g.tiles_per_seq * p.BH;
@@ -589,7 +648,7 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
   p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_fwd);
   p.flags_stride = wl.tiles_per_seq;
-  auto kern = fwd_kernel<D, NQ, NKV, NS>;
+  auto kern = fwd_kernel<D, NQ, NKV, NS, kSplit>;
   const size_t smem = sizeof(FwdSmem<D, NQ, NKV, NS>) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
@@ -605,8 +664,13 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
 int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
                    uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   // single-buffered, two CTAs per SM (measured faster than one double-buffered CTA)
-  if (pr.D == 64) return launch<64, 1, 1, 1>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
-  if (pr.D == 128) return launch<128, 1, 1, 1>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
+  const bool split = pr.b > 128;
+  if (pr.D == 64)
+    return split ? launch<64, 1, 1, 1, true>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream)
+                 : launch<64, 1, 1, 1, false>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
+  if (pr.D == 128)
+    return split ? launch<128, 1, 1, 1, true>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream)
+                 : launch<128, 1, 1, 1, false>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
   return SQB_ERR_UNSUPPORTED;
 }
 

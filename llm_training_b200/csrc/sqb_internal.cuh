@@ -33,6 +33,12 @@ struct WorkspaceLayout {
   size_t delta;       // fp32[B*H*T]   rowsum(dO * O)
   size_t dkbar;       // fp32[B*H*Gc*D] summary-gradient accumulators
   size_t dvbar;       // fp32[B*H*Gc*D]
+  // b > 128 only: fp32[B*H*G*(tpb-1)*128*D] each, the dK / dV contributions of a
+  // block's later sub-tiles to the keys of its earlier sub-tiles
+  size_t dkx, dvx;
+  // b > 128 only: uint32[B*H*G] count of a block's sub-tiles that have read
+  // its summary-gradient sums (the last one re-zeroes them)
+  size_t readers;
   size_t total;
   int tiles_per_seq;  // upper bound on work tiles per (batch, head)
 };
@@ -82,6 +88,17 @@ inline WorkspaceLayout workspace_layout(int64_t B, int64_t T, int64_t H, int64_t
   off = align_up(off, 256);
   w.dvbar = off;
   off += (size_t)BH * Gc * D * 4;
+  const int64_t G = (T + b - 1) / b;
+  const int64_t xrows = b > 128 ? ((b + 127) / 128 - 1) * 128 : 0;  // per block
+  off = align_up(off, 256);
+  w.dkx = off;
+  off += (size_t)BH * G * xrows * D * 4;
+  off = align_up(off, 256);
+  w.dvx = off;
+  off += (size_t)BH * G * xrows * D * 4;
+  off = align_up(off, 256);
+  w.readers = off;
+  off += b > 128 ? (size_t)BH * G * 4 : 0;
   w.total = align_up(off, 256);
   return w;
 }

@@ -51,7 +51,7 @@ bool common_ok(const Problem& p, std::initializer_list<TensorView> views, const 
                const void* kbar, const void* vbar) {
   if (p.dtype != SQB_BF16) return false;
   if (p.D != 64 && p.D != 128) return false;
-  if (p.b % 16 != 0 || p.b < 32 || p.b > 128) return false;
+  if (p.b % 16 != 0 || p.b < 32) return false;
   if (!lse || !aligned16(lse)) return false;
   if (p.Gc > 0 && (!aligned16(kbar) || !aligned16(vbar))) return false;
   for (const TensorView& t : views)
@@ -102,10 +102,10 @@ int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, Te
                   cudaStream_t stream) {
   int num_sms = 0;
   if (!device_ok(&num_sms)) return SQB_ERR_DEVICE;
-  const int R = sm100::tile_rows(p.b);
+  const int R = sm100::tile_rows(p.b), RS = sm100::store_rows(p.b);
   sm100::TensorMaps tm;
   if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) ||
-      !encode_bthd(&tm.v, p, v, R) || !encode_bthd(&tm.o, p, o, R))
+      !encode_bthd(&tm.v, p, v, R) || !encode_bthd(&tm.o, p, o, RS))
     return SQB_ERR_CUDA;
   if (p.Gc > 0) {
     if (!encode_summaries(&tm.kbar, p, kbar) || !encode_summaries(&tm.vbar, p, vbar))
@@ -123,13 +123,13 @@ int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, T
                    const WorkspaceLayout& wl, cudaStream_t stream) {
   int num_sms = 0;
   if (!device_ok(&num_sms)) return SQB_ERR_DEVICE;
-  const int R = sm100::tile_rows(p.b);
+  const int R = sm100::tile_rows(p.b), RS = sm100::store_rows(p.b);
   sm100::BwdTensorMaps tm;
   if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) ||
       !encode_bthd(&tm.v, p, v, R) || !encode_bthd(&tm.o, p, o, R) ||
       !encode_bthd(&tm.dout, p, dout, R) ||
-      !encode_bthd(&tm.dq, p, dq, R) || !encode_bthd(&tm.dk, p, dk, R) ||
-      !encode_bthd(&tm.dv, p, dv, R))
+      !encode_bthd(&tm.dq, p, dq, RS) || !encode_bthd(&tm.dk, p, dk, RS) ||
+      !encode_bthd(&tm.dv, p, dv, RS))
     return SQB_ERR_CUDA;
   if (p.Gc > 0) {
     if (!encode_summaries(&tm.kbar, p, kbar) || !encode_summaries(&tm.vbar, p, vbar))

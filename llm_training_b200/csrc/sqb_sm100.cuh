@@ -30,7 +30,20 @@ int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, T
 namespace sm100 {
 
 // Rows per work tile: 128 when b divides 128 (whole blocks per tile), else b.
-inline int tile_rows(int b) { return (128 % b == 0) ? 128 : b; }
+// Rows of a work tile's load box: 128 when b divides 128 or b > 128 (a block
+// is then split into sub-tiles of up to 128 rows), else b.
+inline int tile_rows(int b) { return (b > 128 || 128 % b == 0) ? 128 : b; }
+// Rows of a store box: a sub-tile shorter than 128 rows (the last one of a
+// block when b > 128) is stored 16 rows at a time, so no store writes rows of
+// the next block's tile.
+inline int store_rows(int b) { return b > 128 ? 16 : tile_rows(b); }
+// Sub-tiles per block and work tiles per (batch, head).
+inline int tiles_per_block(int b) { return b > 128 ? (b + 127) / 128 : 1; }
+inline int tiles_per_seq(int T, int b) {
+  if (b <= 128) return (T + tile_rows(b) - 1) / tile_rows(b);
+  const int G = (T + b - 1) / b;
+  return (G - 1) * tiles_per_block(b) + (T - (G - 1) * b + 127) / 128;
+}
 
 struct TensorMaps {
   CUtensorMap q, k, v, o, kbar, vbar;

@@ -16,38 +16,93 @@ constexpr int kTileRows = 128;    // TMEM lanes / UMMA M
 constexpr int kAtomCols = 64;     // bf16 columns per 128-byte swizzle atom
 constexpr int kAtomBytes = kTileRows * 128;  // one 64-column atom of a 128-row tile
 
-// Work tile: a run of R query rows that starts on a block boundary and holds
-// whole blocks (R = 128 when b divides 128, else R = b, one block per tile).
+// Work tile: a run of query rows that starts on a block boundary.  For
+// b <= 128 a tile holds whole blocks (R = 128 when b divides 128, else R = b,
+// one block per tile).  For b > 128 a block is split into tpb = ceil(b / 128)
+// sub-tiles of up to 128 rows; sub-tile v of a block sees the block's keys in
+// v + 1 in-block chunks of 128: chunks u < v lie wholly before its rows (every
+// key visible), chunk v holds its own rows (causal).
 // Tiles of one (batch, head) sequence are numbered s = 0 .. tiles_per_seq-1.
 struct Geometry {
   int T, b, Gc, R, tiles_per_seq;
+  int tpb;  // sub-tiles per block (b > 128), else 1
 };
 
 struct Tile {
   int s, bh, n, h;  // sequence tile, batch*head, batch, head
-  int r0, rows;     // first row, valid rows (<= R)
+  int r0, rows;     // first row, valid rows (<= 128)
   int blk0;         // first block of the tile
+  int sub;          // sub-tile index within its block (b > 128), else 0
+  int nin;          // in-block chunks: sub + 1
+  int kin0;         // first key row of in-block chunk 0
   int ns;           // summaries the last row sees: min(last block, Gc)
   int nsc;          // summary chunks of <= 128 summaries
-  int n_in;         // MMA N of the in-block chunk (rows rounded up to 16)
+  int n_in;         // MMA N of the diagonal in-block chunk (rows rounded up to 16)
 };
 
 __host__ __device__ inline int round16(int x) { return (x + 15) & ~15; }
 
+// kSplit: the geometry has b > 128 (kernels are compiled for one case or the
+// other, so the b <= 128 path carries no sub-tile logic).
+template <bool kSplit>
 __device__ inline Tile make_tile(const Geometry& g, int H, int s, int bh) {
   Tile t;
   t.s = s;
   t.bh = bh;
   t.n = bh / H;
   t.h = bh % H;
-  t.r0 = s * g.R;
-  t.rows = min(g.R, g.T - t.r0);
-  t.blk0 = t.r0 / g.b;
+  if constexpr (kSplit) {
+    t.blk0 = s / g.tpb;
+    t.sub = s % g.tpb;
+    t.kin0 = t.blk0 * g.b;
+    t.r0 = t.kin0 + t.sub * kTileRows;
+    t.rows = min(min(kTileRows, g.b - t.sub * kTileRows), g.T - t.r0);
+  } else {
+    t.r0 = s * g.R;
+    t.rows = min(g.R, g.T - t.r0);
+    t.blk0 = t.r0 / g.b;
+    t.sub = 0;
+    t.kin0 = t.r0;
+  }
+  t.nin = kSplit ? t.sub + 1 : 1;
   const int last_blk = (t.r0 + t.rows - 1) / g.b;
   t.ns = min(last_blk, g.Gc);
   t.nsc = (t.ns + 127) / 128;
   t.n_in = round16(t.rows);
   return t;
+}
+
+// In-block chunk u of a tile: keys [k0, k0 + n) of the tile's block, MMA width n.
+struct InChunk {
+  int k0, n;
+  bool diag;  // the tile's own rows (causal); otherwise every key is visible
+};
+
+template <bool kSplit>
+__device__ inline InChunk in_chunk(const Tile& t, int u) {
+  InChunk k;
+  if constexpr (!kSplit) {
+    k.k0 = t.r0;
+    k.diag = true;
+    k.n = t.n_in;
+    return k;
+  }
+  k.k0 = t.kin0 + kTileRows * u;
+  k.diag = u == t.nin - 1;
+  k.n = k.diag ? t.n_in : kTileRows;
+  return k;
+}
+
+// Tile (sequence index) whose pooling publishes summary j.
+template <bool kSplit>
+__device__ inline int summary_tile(const Geometry& g, int j) {
+  return kSplit ? j * g.tpb + g.tpb - 1 : (j * g.b) / g.R;
+}
+
+// Number of sub-tiles of block j (the last block of a sequence may be short).
+__device__ inline int block_tiles(const Geometry& g, int j) {
+  const int len = min(g.b, g.T - j * g.b);
+  return (len + kTileRows - 1) / kTileRows;
 }
 
 // Summary chunk c (0-based) covers summaries [128c, e); the 16-row-rounded MMA

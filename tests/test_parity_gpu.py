@@ -119,6 +119,12 @@ def test_golden_fixture_fp32():
     (1, 2, 4096, 128, 64),
     (1, 2, 1000, 128, 128),  # T < ... with a partial block
     (1, 1, 100, 64, 128),    # a single partial block, no summaries at all
+    # b > 128: blocks split into sub-tiles of <= 128 rows
+    (1, 2, 1000, 64, 192),   # 128 + 64 rows per block; last block 40 rows
+    (1, 2, 2000, 128, 144),  # 128 + 16 rows per block; last block one full sub-tile
+    (2, 1, 1100, 128, 256),  # 128 + 128; last block 76 rows
+    (1, 2, 1224, 64, 256),   # last block 200 rows = two sub-tiles
+    (1, 1, 3000, 64, 320),   # three sub-tiles per block (128 + 128 + 64)
 ])
 def test_ragged_and_long_shapes_bf16(impl, B, H, T, D, b):
     q, k, v, do = inputs(B, H, T, D, 7, torch.bfloat16)
