@@ -147,12 +147,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // A tile is claimed when its loads can be issued: Q, dO and O of a tile
-    // load as soon as the previous tile's last MMA has read Q/dO/V
-    // (ld_empty), i.e. during its epilogue.  A tile claimed earlier would
-    // hold back every tile of its sequence that waits for its summary
-    // gradients (measured: claiming one tile ahead, with or without an L2
-    // prefetch of its inputs, is slower).
+    // A tile is claimed when its loads can be issued and it can start: Q, dO
+    // and O of a tile load once the previous tile's last MMA has read
+    // Q/dO/V (ld_empty) and its epilogue has the block sums it waits for
+    // (sums_ready), i.e. during the rest of that epilogue.  A tile claimed
+    // earlier would hold back every tile of its sequence that waits for its
+    // summary gradients (measured: claiming one tile ahead, with or without
+    // an L2 prefetch of its inputs, is slower; claiming before sums_ready
+    // lets waits compound along long sequences).
     if (lane == 0) {
       auto claim = [&]() {
         const int c = (int)atomicAdd(p.ctrl + kBwdTileCounter, 1u);
@@ -163,6 +165,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tc > 0) {
           ptx::mbar_wait(&sm.ld_empty, (tc - 1) & 1, status, 0x50000000u);
           ptx::mbar_wait(&sm.pub_read, (tc - 1) & 1, status, 0x53000000u);
+          // and only once the previous tile's epilogue has everything it
+          // waits for: a tile claimed by a CTA whose gradient warps are
+          // still waiting would start - and publish - late, and the tiles
+          // waiting on it in turn (a convoy on long sequences)
+          ptx::mbar_wait(&sm.sums_ready, (tc - 1) & 1, status, 0x56000000u);
         }
         const int n = claim();
         sm.tile_ring = n;
