@@ -47,9 +47,10 @@ struct BwdParams {
   int64_t o_sb, o_st, o_sh;
   float* dkbar;  // fp32 (BH, Gc, D) accumulators, zero between launches
   float* dvbar;
-  // b > 128: fp32 (BH, G, xrows, D) accumulators of the dK / dV that a block's
-  // later sub-tiles contribute to the keys of its earlier ones (xrows =
-  // (sub-tiles per block - 1) * 128), zero between launches
+  // b > 128: fp32 (BH, G, xrows, D) rows of the dK / dV that a block's later
+  // sub-tiles contribute to the keys of its earlier ones (xrows = (sub-tiles
+  // per block - 1) * 128): stored by the single writer with two sub-tiles per
+  // block, else accumulators that are zero between launches
   float* dkx;
   float* dvx;
   uint32_t* readers;  // b > 128: per (batch*head, block) count of sub-tiles that read its sums
@@ -419,7 +420,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Adds this lane's row of a chunk's dKc / dVc (TMEM, S and dP columns,
       // this warp's column half) to fp32 rows of the workspace with vector
       // atomics, then frees the columns for the next chunk's S/dP.
-      auto drain = [&](float* dkrow, float* dvrow, bool ok) {
+      // store: plain stores instead of atomic additions (a destination with a
+      // single writer)
+      auto drain = [&](float* dkrow, float* dvrow, bool ok, bool store) {
 #pragma unroll 1
         for (int pc = 0; pc < kHalfD / 16; ++pc) {
           const int col0 = half * kHalfD + pc * 16;
@@ -429,7 +432,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tmem_wait_ld();
           ptx::reg_fence(gv);
           ptx::reg_fence(gk);
-          if (ok) {
+          if (ok && store) {
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4) {
+              __stcg(reinterpret_cast<uint4*>(dvrow + col0 + 4 * j4),
+                     make_uint4(gv[4 * j4], gv[4 * j4 + 1], gv[4 * j4 + 2], gv[4 * j4 + 3]));
+              __stcg(reinterpret_cast<uint4*>(dkrow + col0 + 4 * j4),
+                     make_uint4(gk[4 * j4], gk[4 * j4 + 1], gk[4 * j4 + 2], gk[4 * j4 + 3]));
+            }
+          } else if (ok) {
 #pragma unroll
             for (int j4 = 0; j4 < 4; ++j4) {
               ptx::red_add_v4(dvrow + col0 + 4 * j4, __uint_as_float(gv[4 * j4]),
@@ -453,7 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
         const int j = sc.w + row;  // this lane's summary
         const size_t jr = (size_t)t.bh * p.g.Gc + j;
-        drain(p.dkbar + jr * D, p.dvbar + jr * D, row >= sc.lo - sc.w && row < sc.e - sc.w);
+        drain(p.dkbar + jr * D, p.dvbar + jr * D, row >= sc.lo - sc.w && row < sc.e - sc.w,
+              false);
       }
 
       // ---- b > 128: in-block chunks before this sub-tile's rows.  Every key is
@@ -463,7 +475,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = 0; u + 1 < t.nin; ++u) {
         softmax_grad(kTileRows, 0, valid ? kTileRows : 0);
         const size_t xr = ((size_t)t.bh * p.G + t.blk0) * p.xrows + u * kTileRows + row;
-        drain(p.dkx + xr * D, p.dvx + xr * D, true);
+        // with two sub-tiles per block (b <= 256) a key's cross contribution
+        // has one writer: stored, and never re-zeroed (each launch rewrites it
+        // before it is read); with more, added and re-zeroed by the reader
+        drain(p.dkx + xr * D, p.dvx + xr * D, true, p.g.tpb == 2);
       }
 
       // ---- publish (by the publisher warp): this warp's additions are done
@@ -516,11 +531,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               float4* xv = reinterpret_cast<float4*>(p.dvx + xr * D + col);
               const float4 k0 = __ldcg(xk), k1 = __ldcg(xk + 1);
               const float4 v0 = __ldcg(xv), v1 = __ldcg(xv + 1);
-              const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-              __stcg(xk, z);
-              __stcg(xk + 1, z);
-              __stcg(xv, z);
-              __stcg(xv + 1, z);
+              if (p.g.tpb > 2) {
+                const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+                __stcg(xk, z);
+                __stcg(xk + 1, z);
+                __stcg(xv, z);
+                __stcg(xv + 1, z);
+              }
               fk[0] += k0.x; fk[1] += k0.y; fk[2] += k0.z; fk[3] += k0.w;
               fk[4] += k1.x; fk[5] += k1.y; fk[6] += k1.z; fk[7] += k1.w;
               fv[0] += v0.x; fv[1] += v0.y; fv[2] += v0.z; fv[3] += v0.w;

@@ -34,7 +34,8 @@ struct WorkspaceLayout {
   size_t dkbar;       // fp32[B*H*Gc*D] summary-gradient accumulators
   size_t dvbar;       // fp32[B*H*Gc*D]
   // b > 128 only: fp32[B*H*G*(tpb-1)*128*D] each, the dK / dV contributions of a
-  // block's later sub-tiles to the keys of its earlier sub-tiles
+  // block's later sub-tiles to the keys of its earlier sub-tiles (stored when a
+  // block has two sub-tiles, accumulated and re-zeroed when it has more)
   size_t dkx, dvx;
   // b > 128 only: uint32[B*H*G] count of a block's sub-tiles that have read
   // its summary-gradient sums (the last one re-zeroes them)
