@@ -15,7 +15,11 @@
 //   dVc = P^T dO, dKc = dS^T Q                       (TMEM, lanes = keys)
 //   dQ += dS Kc                                      (TMEM, lanes = queries)
 // For a summary chunk, dKc/dVc are summary gradients: they are added with
-// fp32 vector atomics into per-(batch, head) accumulators in the workspace.
+// fp32 atomics into per-(batch, head) accumulators in the workspace.  For
+// D = 128 they are computed transposed (dVbar^T = dO^T P, dKbar^T = Q^T dS:
+// TMEM lanes = feature, columns = summaries), so each warp's atomic covers
+// 32 consecutive features of one summary - one 128-byte row segment - instead
+// of 32 summary rows.
 // For the in-block chunk they are the tile's own dK/dV, to which the epilogue
 // adds (summary gradient of the key's block) / b - a summary is the mean of
 // its block - before storing dK, dV and dQ through smem with TMA.
@@ -69,7 +73,9 @@ struct BwdSmem {
   alignas(1024) uint8_t k[kTileBytes];     // K chunk, then dQ staging
   alignas(1024) uint8_t v[kTileBytes];     // O (for delta), then the V chunk
   alignas(1024) uint8_t p[2 * kAtomBytes];   // P (128 query rows x 128 keys), then dK staging
-  alignas(1024) uint8_t ds[2 * kAtomBytes];  // dS (same layout), then dV staging
+  // dS (same layout), then dV staging; the first summary chunk's Vbar is
+  // loaded here (the tile's O still occupies the V buffer until delta is done)
+  alignas(1024) uint8_t ds[2 * kAtomBytes];
   float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
   uint64_t ld_full, ld_empty, k_full, k_empty, v_full, v_empty, s_full, ps_full, g_full, g_free;
   uint64_t delta_done, stage_free;
@@ -105,6 +111,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* status = p.ctrl + kStatus;
   const uint32_t token = *reinterpret_cast<volatile uint32_t*>(p.ctrl + kBwdEpoch) + 1u;
   constexpr int kAtoms = D / 64;
+  // summary gradients with TMEM lanes = features (needs M = D = 128)
+  constexpr bool kTransposedSums = D == 128;
   const uint32_t box_bytes = (uint32_t)p.g.R * 128u;
   const int NT = p.g.tiles_per_seq;
 
@@ -194,6 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // to be read by its TMA store; its first V load waits for delta,
         // which reads O from the V buffer.
         const int nch = t.nsc + t.nin;  // summary chunks, then in-block chunks
+        // the first chunk loaded into the V buffer waits for delta (O is there)
+        const int first_v = t.nsc > 0 ? 1 : 0;
         for (int c = 0; c < nch; ++c) {
           auto load_k = [&]() {
             ptx::mbar_wait(&sm.k_empty, (kc & 1) ^ 1, status, 0x51000000u);
@@ -216,13 +226,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           };
           auto load_v = [&]() {
             ptx::mbar_wait(&sm.v_empty, (kc & 1) ^ 1, status, 0x55000000u);
-            if (c == 0) ptx::mbar_wait(&sm.delta_done, tc & 1, status, 0x52000000u);
+            if (c == first_v) ptx::mbar_wait(&sm.delta_done, tc & 1, status, 0x52000000u);
             if (c < t.nsc) {
+              // chunk 0 into the dS buffer, free since the previous tile's
+              // staging was read (stage_free, waited for by load_k above)
               const SumChunk sc = sum_chunk(t, c);
+              uint8_t* dst = c == 0 ? sm.ds : sm.v;
               ptx::mbar_arrive_expect_tx(&sm.v_full, kAtoms * kAtomBytes);
 #pragma unroll
               for (int a = 0; a < kAtoms; ++a)
-                ptx::tma_load_3d(sm.v + a * kAtomBytes, &tm_vbar, &sm.v_full, a * 64, sc.w, t.bh);
+                ptx::tma_load_3d(dst + a * kAtomBytes, &tm_vbar, &sm.v_full, a * 64, sc.w, t.bh);
             } else {
               const InChunk ic = in_chunk<kSplit>(t, c - t.nsc);
               ptx::mbar_arrive_expect_tx(&sm.v_full, kAtoms * box_bytes);
@@ -233,8 +246,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           };
           // in the order their buffers free up: for a tile's first chunk K
-          // (previous tile's store read) before V (this tile's delta), for
-          // later chunks V (previous dP) before K (previous dQ)
+          // (previous tile's store read) before V (the same store read for a
+          // summary chunk, else this tile's delta), for later chunks V
+          // (previous dP) before K (previous dQ)
           if (c == 0) {
             load_k();
             load_v();
@@ -275,9 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kk > 0 ? 1u : 0u);
           ptx::mbar_wait(&sm.v_full, kc & 1, status, 0x64000000u);
           ptx::tc_fence_after();
+          const uint32_t vc_s = (c == 0 && t.nsc > 0) ? ds_s : v_s;  // where this chunk's V is
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            ptx::mma_ss(tmem + kColDP, desc_kmajor(do_s, kk), desc_kmajor(v_s, kk), idesc_s,
+            ptx::mma_ss(tmem + kColDP, desc_kmajor(do_s, kk), desc_kmajor(vc_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
           ptx::mma_commit(&sm.s_full);
           ptx::mma_commit(&sm.v_empty);  // the V chunk is read only by dP
@@ -287,12 +302,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
                         (c > 0 || kk > 0) ? 1u : 0u);
           ptx::mma_commit(&sm.k_empty);
-          for (int kk = 0; kk < kq; ++kk)  // dVc = P^T dO
-            ptx::mma_ss(tmem + kColS, desc_mnmajor(p_s, kk), desc_mnmajor(do_s, kk), idesc_dvdk,
-                        kk > 0 ? 1u : 0u);
-          for (int kk = 0; kk < kq; ++kk)  // dKc = dS^T Q
-            ptx::mma_ss(tmem + kColDP, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
-                        kk > 0 ? 1u : 0u);
+          if (kTransposedSums && c < t.nsc) {
+            // summary gradients transposed (D = 128 = M): all 128 columns of
+            // P / dS, zero outside the chunk's visible summaries
+            for (int kk = 0; kk < kq; ++kk)  // dVc^T = dO^T P
+              ptx::mma_ss(tmem + kColS, desc_mnmajor(do_s, kk), desc_mnmajor(p_s, kk), idesc_dvdk,
+                          kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kq; ++kk)  // dKc^T = Q^T dS
+              ptx::mma_ss(tmem + kColDP, desc_mnmajor(q_s, kk), desc_mnmajor(ds_s, kk), idesc_dvdk,
+                          kk > 0 ? 1u : 0u);
+          } else {
+            for (int kk = 0; kk < kq; ++kk)  // dVc = P^T dO
+              ptx::mma_ss(tmem + kColS, desc_mnmajor(p_s, kk), desc_mnmajor(do_s, kk), idesc_dvdk,
+                          kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kq; ++kk)  // dKc = dS^T Q
+              ptx::mma_ss(tmem + kColDP, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
+                          kk > 0 ? 1u : 0u);
+          }
           ptx::mma_commit(&sm.g_full);
           if (c == nch - 1) ptx::mma_commit(&sm.ld_empty);  // Q, dO, V no longer read
           ++kc;
@@ -458,14 +484,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kc;
       };
 
+      // Transposed summary chunk (D = 128): this lane holds feature d = row of
+      // the chunk's summaries in columns; one scalar atomic per summary, and
+      // each warp instruction covers 32 consecutive features of one summary.
+      auto drain_sums_t = [&](const SumChunk& sc) {
+        const int clo = sc.lo - sc.w, chi = sc.e - sc.w;  // columns of real summaries
+        float* dvb = p.dvbar + (size_t)t.bh * p.g.Gc * D + row;
+        float* dkb = p.dkbar + (size_t)t.bh * p.g.Gc * D + row;
+#pragma unroll 1
+        for (int pc = 0; pc < 4; ++pc) {
+          const int col0 = half * 64 + pc * 16;
+          if (col0 + 16 <= clo || col0 >= chi) continue;  // warp-uniform
+          uint32_t gv[16], gk[16];
+          ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
+          ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence(gv);
+          ptx::reg_fence(gk);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int col = col0 + jj;
+            if (col >= clo && col < chi) {
+              const size_t off = (size_t)(sc.w + col) * D;
+              ptx::red_add_f32(dvb + off, __uint_as_float(gv[jj]));
+              ptx::red_add_f32(dkb + off, __uint_as_float(gk[jj]));
+            }
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+        ++kc;
+      };
+
       // ---- summary chunks: add dKc / dVc to the summary accumulators
       for (int c = 0; c < t.nsc; ++c) {
         const SumChunk sc = sum_chunk(t, c);
         softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
-        const int j = sc.w + row;  // this lane's summary
-        const size_t jr = (size_t)t.bh * p.g.Gc + j;
-        drain(p.dkbar + jr * D, p.dvbar + jr * D, row >= sc.lo - sc.w && row < sc.e - sc.w,
-              false);
+        if constexpr (kTransposedSums) {
+          drain_sums_t(sc);
+        } else {
+          const int j = sc.w + row;  // this lane's summary
+          const size_t jr = (size_t)t.bh * p.g.Gc + j;
+          drain(p.dkbar + jr * D, p.dvbar + jr * D, row >= sc.lo - sc.w && row < sc.e - sc.w,
+                false);
+        }
       }
 
       // ---- b > 128: in-block chunks before this sub-tile's rows.  Every key is

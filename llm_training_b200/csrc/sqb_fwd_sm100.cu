@@ -14,7 +14,10 @@
 //   O += P V             tcgen05.mma, A = P from TMEM (bf16), B = V smem
 // The online softmax spans both kinds of chunk, so in-block keys and
 // summaries share one softmax.  LSE (natural log) and O are written at the
-// end; O goes through smem and a TMA store.
+// end.  O leaves through a small per-warp transpose buffer (32 rows x 64
+// bytes) with coalesced global stores, so no operand buffer is held by the
+// epilogue and the next tile's K/V loads - and with them its pooling and the
+// summary flags later tiles wait on - are never delayed by an O store.
 //
 // Summaries cross CTAs: tiles are handed out in ascending sequence order
 // (tile index n -> s = n / BH), the pooling warps of tile s publish their
@@ -41,10 +44,11 @@ struct FwdParams {
   __nv_bfloat16* kbar;
   __nv_bfloat16* vbar;
   float* lse;
+  __nv_bfloat16* o;
+  int64_t o_sb, o_st, o_sh;  // element strides of O (batch, token, head)
   uint32_t* ctrl;
   uint32_t* flags;
   int flags_stride;
-  int store_rows;  // rows per O store box
 };
 
 // Pipeline depths: NQ query-tile slots, NKV key/value chunk stages, NS score
@@ -58,9 +62,10 @@ struct FwdSmem {
   alignas(1024) uint8_t k[NKV][kTileBytes];
   alignas(1024) uint8_t v[NKV][kTileBytes];
   float red[4][2][D];
+  // per softmax warp: 32 rows x 32 columns of O (bf16), 16-byte chunks swizzled
+  alignas(16) uint8_t ostage[4][32 * 64];
   uint64_t q_full[NQ], q_empty[NQ];
   uint64_t k_full[NKV], k_empty[NKV], v_full[NKV], v_empty[NKV];
-  uint64_t vbuf_free;  // pooling done with a tile's last V chunk: O may be staged there
   uint64_t s_full[NS], p_full[NS], s_free[NS], o_full, o_free;
   int tile_ring[NQ];
   uint32_t tmem_base;
@@ -92,8 +97,7 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 q) {
 template <int D, int NQ, int NKV, int NS, bool kSplit>
 __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-               const __grid_constant__ CUtensorMap tm_kbar,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kbar,
                const __grid_constant__ CUtensorMap tm_vbar, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   FwdSmem<D, NQ, NKV, NS>& sm = *reinterpret_cast<FwdSmem<D, NQ, NKV, NS>*>(
@@ -115,9 +119,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       ptx::mbar_init(&sm.k_full[i], 1);
       ptx::mbar_init(&sm.k_empty[i], 2);  // S mma complete + pooling done
       ptx::mbar_init(&sm.v_full[i], 1);
-      // PV mma complete + pooling done (for a tile's last chunk, whose
-      // buffer stages O: + the O store's read)
-      ptx::mbar_init(&sm.v_empty[i], 2);
+      ptx::mbar_init(&sm.v_empty[i], 2);  // PV mma complete + pooling done
     }
     for (int i = 0; i < NS; ++i) {
       ptx::mbar_init(&sm.s_full[i], 1);
@@ -126,14 +128,12 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     }
     ptx::mbar_init(&sm.o_full, 1);
     ptx::mbar_init(&sm.o_free, 4);
-    ptx::mbar_init(&sm.vbuf_free, 1);
     ptx::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
     ptx::tma_prefetch_desc(&tm_q);
     ptx::tma_prefetch_desc(&tm_k);
     ptx::tma_prefetch_desc(&tm_v);
-    ptx::tma_prefetch_desc(&tm_o);
   }
   if (warp == 1) {
     ptx::tmem_alloc(&sm.tmem_base, kTmemCols);
@@ -429,59 +429,55 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&sm.p_full[x]);
       }
-      // ---- epilogue: O / l -> bf16 -> swizzled smem -> TMA store.  O is
-      // staged in the V buffer of the tile's last chunk: its last reader, PV,
-      // has completed (o_full) and pooling has finished with it (vbuf_free),
-      // while the Q slot is already taken by the next tile.
+      // ---- epilogue: O / l -> bf16, 32 columns at a time through the warp's
+      // transpose buffer: each lane writes its row's 64 bytes, then reads 16
+      // bytes of row 8i + lane/4, so one store instruction covers 8 rows x 64
+      // contiguous bytes instead of 32 rows x 16 bytes.
       ptx::mbar_wait(&sm.o_full, tc & 1, status, 0x33000000u);
       ptx::tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      const int vst = (gc + nch - 1) % NKV;
-      uint8_t* stage = sm.v[vst];
-      ptx::mbar_wait(&sm.vbuf_free, tc & 1, status, 0x34000000u);
-      auto emit = [&](const uint32_t (&r)[32], int pc) {
-#pragma unroll
-        for (int j8 = 0; j8 < 4; ++j8) {
-          uint4 w;
-          w.x = ptx::pack_bf16x2(__uint_as_float(r[8 * j8 + 0]) * inv_l,
-                                 __uint_as_float(r[8 * j8 + 1]) * inv_l);
-          w.y = ptx::pack_bf16x2(__uint_as_float(r[8 * j8 + 2]) * inv_l,
-                                 __uint_as_float(r[8 * j8 + 3]) * inv_l);
-          w.z = ptx::pack_bf16x2(__uint_as_float(r[8 * j8 + 4]) * inv_l,
-                                 __uint_as_float(r[8 * j8 + 5]) * inv_l);
-          w.w = ptx::pack_bf16x2(__uint_as_float(r[8 * j8 + 6]) * inv_l,
-                                 __uint_as_float(r[8 * j8 + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(stage + swz_offset(row, pc * 32 + j8 * 8)) = w;
-        }
-      };
+      uint8_t* ost = sm.ostage[quarter];
+      const int rsub = lane >> 2, csub = lane & 3;  // read-back: row in an 8-row group, chunk
+      const int64_t o_rows0 = (int64_t)t.n * p.o_sb + (int64_t)t.h * p.o_sh;
 #pragma unroll 1
       for (int pc = 0; pc < D / 32; ++pc) {
         uint32_t r0[32];
         ptx::tmem_ld32(o_addr + pc * 32, r0);
         ptx::tmem_wait_ld();
         ptx::reg_fence(r0);
-        emit(r0, pc);
+#pragma unroll
+        for (int j8 = 0; j8 < 4; ++j8) {
+          uint4 w;
+          w.x = ptx::pack_bf16x2(__uint_as_float(r0[8 * j8 + 0]) * inv_l,
+                                 __uint_as_float(r0[8 * j8 + 1]) * inv_l);
+          w.y = ptx::pack_bf16x2(__uint_as_float(r0[8 * j8 + 2]) * inv_l,
+                                 __uint_as_float(r0[8 * j8 + 3]) * inv_l);
+          w.z = ptx::pack_bf16x2(__uint_as_float(r0[8 * j8 + 4]) * inv_l,
+                                 __uint_as_float(r0[8 * j8 + 5]) * inv_l);
+          w.w = ptx::pack_bf16x2(__uint_as_float(r0[8 * j8 + 6]) * inv_l,
+                                 __uint_as_float(r0[8 * j8 + 7]) * inv_l);
+          *reinterpret_cast<uint4*>(ost + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = w;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = 8 * i + rsub;  // row of this warp's 32
+          const uint4 w =
+              *reinterpret_cast<const uint4*>(ost + r * 64 + ((csub ^ ((r >> 1) & 3)) << 4));
+          if (quarter * 32 + r < t.rows)
+            *reinterpret_cast<uint4*>(p.o + o_rows0 +
+                                      (int64_t)(t.r0 + quarter * 32 + r) * p.o_st + pc * 32 +
+                                      csub * 8) = w;
+        }
+        __syncwarp();
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&sm.o_free);
       if (valid) p.lse[(size_t)t.bh * p.g.T + tq] = (m + __log2f(l)) * kLn2;
-      ptx::fence_proxy_async_smem();
-      ptx::named_barrier(1, 128);
-      if (warp == 2 && lane == 0) {
-#pragma unroll
-        for (int a = 0; a < kAtoms; ++a)
-          for (int r = 0; r < t.rows; r += p.store_rows)
-            ptx::tma_store_4d(&tm_o, stage + a * kAtomBytes + r * 128, a * 64, t.h, t.r0 + r,
-                              t.n);
-        ptx::tma_store_commit();
-        ptx::tma_store_wait_read_all();
-        ptx::mbar_arrive(&sm.v_empty[vst]);
-      }
       gc += nch;
       ++tc;
     }
-    if (warp == 2 && lane == 0) ptx::tma_store_wait_all();
   } else {
     // ------------------------------------------------------------ pooling
     const int ptid = threadIdx.x - 192;  // 0..127
@@ -512,8 +508,6 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         for (int u = 0; u < t.nin; ++u) {
           const int st = kc % NKV;
           const int urows = u == t.nin - 1 ? t.rows : kTileRows;
-          // the tile's last chunk: its V buffer stages O (see the epilogue)
-          const bool last = u == t.nin - 1 && t.nsc == 0;
           // K then V: each buffer is released as soon as its own sums are read,
           // so the next chunk's K load can start while V is still pooled.
 #pragma unroll 1
@@ -558,8 +552,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
             }
             ptx::named_barrier(2, 128);
             if (ptid == 0)
-              ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st]
-                                       : (last ? &sm.vbuf_free : &sm.v_empty[st]));
+              ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st] : &sm.v_empty[st]);
           }
           ++kc;
         }
@@ -599,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
           ptx::mbar_wait(&sm.k_full[st], (kc / NKV) & 1, status, 0x42000000u | st);
           ptx::mbar_arrive(&sm.k_empty[st]);
           ptx::mbar_wait(&sm.v_full[st], (kc / NKV) & 1, status, 0x44000000u | st);
-          ptx::mbar_arrive(c == t.nsc - 1 ? &sm.vbuf_free : &sm.v_empty[st]);
+          ptx::mbar_arrive(&sm.v_empty[st]);
         }
         ++kc;
       }
@@ -628,8 +621,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
 }
 
 template <int D, int NQ, int NKV, int NS, bool kSplit>
-int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
-           uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
+int launch(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, void* kbar,
+           void* vbar, uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   FwdParams p;
   p.g.T = pr.T;
   p.g.b = pr.b;
@@ -637,7 +630,6 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
   p.g.R = tile_rows(pr.b);
   p.g.tiles_per_seq = tiles_per_seq(pr.T, pr.b);
   p.g.tpb = tiles_per_block(pr.b);
-  p.store_rows = store_rows(pr.b);
   p.H = pr.H;
   p.BH = pr.B * pr.H;
   p.total_tiles = p.g.tiles_per_seq * p.BH;
@@ -645,6 +637,10 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
   p.kbar = reinterpret_cast<__nv_bfloat16*>(kbar);
   p.vbar = reinterpret_cast<__nv_bfloat16*>(vbar);
   p.lse = lse;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.ptr);
+  p.o_sb = o.sb;
+  p.o_st = o.st;
+  p.o_sh = o.sh;
   p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_fwd);
   p.flags_stride = wl.tiles_per_seq;
@@ -655,22 +651,23 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
     return SQB_ERR_LAUNCH;
   const int slots = num_sms * ctas_per_sm<NQ, NKV, NS>();
   const int grid = p.total_tiles < slots ? p.total_tiles : slots;
-  kern<<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.kbar, tm.vbar, p);
+  kern<<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kbar, tm.vbar, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 
 }  // namespace
 
-int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
-                   uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
+int launch_forward(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, void* kbar,
+                   void* vbar, uint8_t* ws, const WorkspaceLayout& wl, int num_sms,
+                   cudaStream_t stream) {
   // single-buffered, two CTAs per SM (measured faster than one double-buffered CTA)
   const bool split = pr.b > 128;
   if (pr.D == 64)
-    return split ? launch<64, 1, 1, 1, true>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream)
-                 : launch<64, 1, 1, 1, false>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
+    return split ? launch<64, 1, 1, 1, true>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream)
+                 : launch<64, 1, 1, 1, false>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream);
   if (pr.D == 128)
-    return split ? launch<128, 1, 1, 1, true>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream)
-                 : launch<128, 1, 1, 1, false>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
+    return split ? launch<128, 1, 1, 1, true>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream)
+                 : launch<128, 1, 1, 1, false>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream);
   return SQB_ERR_UNSUPPORTED;
 }
 

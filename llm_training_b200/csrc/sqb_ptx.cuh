@@ -220,6 +220,10 @@ __device__ __forceinline__ bool counters_wait_range(const uint32_t* ctr, int lo,
 }
 
 // Fire-and-forget fp32 vector add into global memory (no value returned).
+__device__ __forceinline__ void red_add_f32(float* addr, float a) {
+  asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(addr), "f"(a) : "memory");
+}
+
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
   asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a),
                "f"(b), "f"(c), "f"(d)

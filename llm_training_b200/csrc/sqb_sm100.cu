@@ -102,10 +102,9 @@ int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, Te
                   cudaStream_t stream) {
   int num_sms = 0;
   if (!device_ok(&num_sms)) return SQB_ERR_DEVICE;
-  const int R = sm100::tile_rows(p.b), RS = sm100::store_rows(p.b);
+  const int R = sm100::tile_rows(p.b);
   sm100::TensorMaps tm;
-  if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) ||
-      !encode_bthd(&tm.v, p, v, R) || !encode_bthd(&tm.o, p, o, RS))
+  if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) || !encode_bthd(&tm.v, p, v, R))
     return SQB_ERR_CUDA;
   if (p.Gc > 0) {
     if (!encode_summaries(&tm.kbar, p, kbar) || !encode_summaries(&tm.vbar, p, vbar))
@@ -114,7 +113,7 @@ int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, Te
     tm.kbar = tm.k;  // never read: a sequence shorter than one block has no summaries
     tm.vbar = tm.v;
   }
-  return sm100::launch_forward(p, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
+  return sm100::launch_forward(p, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream);
 }
 
 int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,

@@ -46,11 +46,12 @@ inline int tiles_per_seq(int T, int b) {
 }
 
 struct TensorMaps {
-  CUtensorMap q, k, v, o, kbar, vbar;
+  CUtensorMap q, k, v, kbar, vbar;
 };
 
-int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
-                   uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream);
+int launch_forward(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, void* kbar,
+                   void* vbar, uint8_t* ws, const WorkspaceLayout& wl, int num_sms,
+                   cudaStream_t stream);
 
 struct BwdTensorMaps {
   CUtensorMap q, k, v, o, dout, dq, dk, dv, kbar, vbar;
