@@ -80,6 +80,7 @@ struct BwdSmem {
   uint64_t ld_full, ld_empty, k_full, k_empty, v_full, v_empty, s_full, ps_full, g_full, g_free;
   uint64_t delta_done, stage_free;
   uint64_t red_done, pub_read, sums_ready, sgrad_free;
+  uint64_t mma_done;  // exit: every MMA of the CTA has completed
   int tile_ring;
   uint32_t tmem_base;
 };
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(&sm.ps_full, 8);
     ptx::mbar_init(&sm.g_full, 1);
     ptx::mbar_init(&sm.g_free, 8);
+    ptx::mbar_init(&sm.mma_done, 1);
     ptx::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -183,6 +185,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n = claim();
         sm.tile_ring = n;
         if (n < 0) {
+          // the copies issued so far have landed (they normally have: after a
+          // failed wait they may still be in flight)
+          if (tc > 0) ptx::mbar_drain(&sm.ld_full, (tc - 1) & 1);
+          if (kc > 0) {
+            ptx::mbar_drain(&sm.k_full, (kc - 1) & 1);
+            ptx::mbar_drain(&sm.v_full, (kc - 1) & 1);
+          }
           ptx::mbar_arrive(&sm.ld_full);
           break;
         }
@@ -325,6 +334,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++tc;
       }
+      // every MMA issued has completed before TMEM is released
+      ptx::mma_commit(&sm.mma_done);
+      ptx::mbar_drain(&sm.mma_done, 0);
     }
   } else if (warp < 10) {
     // ------------------------------------------------------------ gradient warps

@@ -67,6 +67,7 @@ struct FwdSmem {
   uint64_t q_full[NQ], q_empty[NQ];
   uint64_t k_full[NKV], k_empty[NKV], v_full[NKV], v_empty[NKV];
   uint64_t s_full[NS], p_full[NS], s_free[NS], o_full, o_free;
+  uint64_t mma_done;  // exit: every MMA of the CTA has completed
   int tile_ring[NQ];
   uint32_t tmem_base;
 };
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     }
     ptx::mbar_init(&sm.o_full, 1);
     ptx::mbar_init(&sm.o_free, 4);
+    ptx::mbar_init(&sm.mma_done, 1);
     ptx::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -168,7 +170,17 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       const int n = claim();
       if (lane == 0) {
         sm.tile_ring[slot] = n;
-        if (n < 0) ptx::mbar_arrive(&sm.q_full[slot]);
+        if (n < 0) {
+          // the copies issued so far have landed (they normally have: after a
+          // failed wait they may still be in flight)
+          for (int i = 1; i <= NQ && i <= tc; ++i)
+            ptx::mbar_drain(&sm.q_full[(tc - i) % NQ], ((tc - i) / NQ) & 1);
+          for (int i = 1; i <= NKV && i <= kc; ++i) {
+            ptx::mbar_drain(&sm.k_full[(kc - i) % NKV], ((kc - i) / NKV) & 1);
+            ptx::mbar_drain(&sm.v_full[(kc - i) % NKV], ((kc - i) / NKV) & 1);
+          }
+          ptx::mbar_arrive(&sm.q_full[slot]);
+        }
       }
       if (n < 0) break;
       const Tile t = make_tile<kSplit>(p.g, p.H, n / p.BH, n % p.BH);
@@ -293,6 +305,9 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         kc += nch;
         ++tc;
       }
+      // every MMA issued has completed before TMEM is released
+      ptx::mma_commit(&sm.mma_done);
+      ptx::mbar_drain(&sm.mma_done, 0);
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------ softmax

@@ -102,6 +102,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// Exit-path wait for a kernel's own asynchronous work (its TMA copies and
+// MMAs) before shared memory and TMEM are released.  Unlike mbar_wait it does
+// not give up because another wait failed - after a failure the copies
+// already issued still land in shared memory - but it is bounded all the same.
+constexpr uint64_t kDrainBudgetNs = 200000000ull;  // 0.2 s
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > kDrainBudgetNs) return;
+}
+
 // ---- global flags (inter-CTA) -------------------------------------------------
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
