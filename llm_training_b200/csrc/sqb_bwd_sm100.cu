@@ -81,6 +81,7 @@ struct BwdSmem {
   uint64_t delta_done, stage_free;
   uint64_t red_done, pub_read, sums_ready, sgrad_free;
   uint64_t mma_done;  // exit: every MMA of the CTA has completed
+  uint64_t dq_full;   // the tile's dQ accumulation is complete
   int tile_ring;
   uint32_t tmem_base;
 };
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(&sm.g_full, 1);
     ptx::mbar_init(&sm.g_free, 8);
     ptx::mbar_init(&sm.mma_done, 1);
+    ptx::mbar_init(&sm.dq_full, 1);
     ptx::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -206,7 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // K and V buffers are refilled independently: V as soon as the
         // previous chunk's dP has read it, K once its dQ has (the MMA warp
-        // issues dQ first among a chunk's gradient MMAs).  A tile's first K
+        // issues dQ last among a chunk's gradient MMAs, so the drain and the
+        // epilogue of dK/dV start first).  A tile's first K
         // load also waits for the previous tile's dQ staging in the K buffer
         // to be read by its TMA store; its first V load waits for delta,
         // which reads O from the V buffer.
@@ -307,10 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::mma_commit(&sm.v_empty);  // the V chunk is read only by dP
           ptx::mbar_wait(&sm.ps_full, kc & 1, status, 0x63000000u);
           ptx::tc_fence_after();
-          for (int kk = 0; kk < N / 16; ++kk)  // dQ += dS Kc (first: frees the K buffer)
-            ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
-                        (c > 0 || kk > 0) ? 1u : 0u);
-          ptx::mma_commit(&sm.k_empty);
+          // dVc / dKc first: their drain (or the epilogue) starts while dQ runs
           if (kTransposedSums && c < t.nsc) {
             // summary gradients transposed (D = 128 = M): all 128 columns of
             // P / dS, zero outside the chunk's visible summaries
@@ -330,6 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::mma_commit(&sm.g_full);
           if (c == nch - 1) ptx::mma_commit(&sm.ld_empty);  // Q, dO, V no longer read
+          for (int kk = 0; kk < N / 16; ++kk)  // dQ += dS Kc
+            ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
+                        (c > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_commit(&sm.k_empty);
+          if (c == nch - 1) ptx::mma_commit(&sm.dq_full);
           ++kc;
         }
         ++tc;
@@ -564,6 +569,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       softmax_grad(t.n_in, valid ? max(0, blk_t * p.g.b - t.r0) : 0, valid ? row + 1 : 0);
       // the publisher has staged sum / b of the tile's complete blocks
       ptx::mbar_wait(&sm.sums_ready, tc & 1, status, 0x73000000u);
+      // dQ (the tile's last MMA) has read dS: the dS buffer may take dV staging
+      ptx::mbar_wait(&sm.dq_full, tc & 1, status, 0x76000000u);
+      ptx::tc_fence_after();
       {
         const bool complete = valid && blk_t < p.g.Gc;  // this lane's key is in a full block
         const int lb_t = valid ? blk_t - t.blk0 : 0;
