@@ -103,6 +103,40 @@ int sqb_bwd(const void* q, const void* k, const void* v, const void* o,
             int64_t block, const int64_t* strides, int dtype, float scale, int impl,
             void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Reference-semantics mode ---------------------------------------------
+ * The attention core of the reference's registered sqrt_block / custom module
+ * itself (model/custom_attention.py:138): T = G * L tokens with G = L = sqrt(T)
+ * (block_geometry, custom_attention.py:68-79, T must be a perfect square);
+ * local_i = causal softmax of Q_i K_i^T * scale inside block i (:195-198);
+ * summary_i = column sums of local_i (:203); glob = softmax over strictly
+ * earlier blocks of summary_i . summary_j / sqrt(L), row 0 zero (:209-213);
+ * out_i = local_i V_i + sum_{j<i} glob[i, j] local_j V_j (_ScaledBlockCombine,
+ * :82-135).  CUDA-core kernels, fp32 arithmetic for fp32 and bf16 inputs,
+ * L <= 64 and D <= 128.  Layout conventions as above.  A T that is not a
+ * perfect square returns SQB_ERR_ARG (the reference raises ValueError). */
+
+/* Bytes of scratch workspace a (B, T, H, D) reference-semantics problem needs
+ * (0 when unsupported).  Its contents need no initialisation. */
+size_t sqb_refsem_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t D);
+
+/* Forward.  strides: 12 int64 = (batch, token, head) for q, k, v, o.  Writes o,
+ * glob (B, H, G, G) fp32 and summary (B, H, G, L) fp32, both contiguous and
+ * saved for the backward.  Replaces model/custom_attention.py:183-227. */
+int sqb_refsem_fwd(const void* q, const void* k, const void* v, void* o, float* glob,
+                   float* summary, int64_t B, int64_t T, int64_t H, int64_t D,
+                   const int64_t* strides, int dtype, float scale, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Backward.  strides: 21 int64 = (batch, token, head) for q, k, v, dout, dq,
+ * dk, dv.  Writes dq, dk, dv (overwritten).  Replaces the autograd backward of
+ * model/custom_attention.py:195-225 (_ScaledBlockCombine.backward :111-135 and
+ * the softmax / summary backward around it). */
+int sqb_refsem_bwd(const void* q, const void* k, const void* v, const void* dout,
+                   const float* glob, const float* summary, void* dq, void* dk, void* dv,
+                   int64_t B, int64_t T, int64_t H, int64_t D, const int64_t* strides,
+                   int dtype, float scale, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
 /* Backward without a caller-supplied workspace.  This entry point has no
  * counterpart in the reference.  It is for callers that cannot allocate device
  * memory where they run the backward (their memory is owned by another

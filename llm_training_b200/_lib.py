@@ -43,6 +43,13 @@ SIGNATURES = {
     "sqb_bwd_noalloc": (ctypes.c_int, [_vp] * 11 + [_c_i64] * 5 + [ctypes.POINTER(_c_i64),
                                                                     ctypes.c_int, ctypes.c_float,
                                                                     ctypes.c_int, _vp]),
+    "sqb_refsem_workspace_bytes": (ctypes.c_size_t, [_c_i64] * 4),
+    "sqb_refsem_fwd": (ctypes.c_int, [_vp] * 6 + [_c_i64] * 4 + [ctypes.POINTER(_c_i64),
+                                                                 ctypes.c_int, ctypes.c_float,
+                                                                 _vp, ctypes.c_size_t, _vp]),
+    "sqb_refsem_bwd": (ctypes.c_int, [_vp] * 9 + [_c_i64] * 4 + [ctypes.POINTER(_c_i64),
+                                                                 ctypes.c_int, ctypes.c_float,
+                                                                 _vp, ctypes.c_size_t, _vp]),
 }
 
 _lock = threading.Lock()

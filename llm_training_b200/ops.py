@@ -17,7 +17,7 @@ import torch
 from . import _lib
 
 __all__ = ["sqrt_block_attention", "sqrt_block_forward", "sqrt_block_backward", "read_status",
-           "block_geometry"]
+           "block_geometry", "reference_attention", "reference_forward", "reference_backward"]
 
 _DTYPES = {torch.float32: _lib.SQB_F32, torch.bfloat16: _lib.SQB_BF16}
 
@@ -173,3 +173,112 @@ class _SqrtBlockAttention(torch.autograd.Function):
 def sqrt_block_attention(q, k, v, block=None, scale=None, impl="auto"):
     """Differentiable sqrt-block attention on (B, T, H, D) CUDA views -> O (B, T, H, D)."""
     return _SqrtBlockAttention.apply(q, k, v, block, scale, impl)
+
+
+# ---- reference-semantics mode ---------------------------------------------------
+
+_refsem_workspaces: dict[tuple, torch.Tensor] = {}
+
+
+def _refsem_workspace(device: torch.device, shape: tuple) -> torch.Tensor:
+    """Scratch for one (B, T, H, D) reference-semantics problem (no initialisation needed)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx,) + tuple(int(x) for x in shape)
+    with _ws_lock:
+        ws = _refsem_workspaces.get(key)
+        if ws is None:
+            nbytes = int(_lib.lib().sqb_refsem_workspace_bytes(*shape))
+            if nbytes == 0:
+                raise ValueError(f"reference-semantics attention does not support (B, T, H, D) = "
+                                 f"{tuple(shape)} (T must be a perfect square with sqrt(T) <= 64, "
+                                 "D <= 128)")
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            _refsem_workspaces[key] = ws
+        return ws
+
+
+def _refsem_check_T(T: int) -> int:
+    L = math.isqrt(max(T, 0))
+    if L * L != T or T <= 0:
+        # the reference's block_geometry (model/custom_attention.py:75-77)
+        raise ValueError(f"sequence length {T} must be a perfect square")
+    return L
+
+
+def reference_forward(q, k, v, scale=None):
+    """Reference-semantics forward -> (o, glob, summary).
+
+    The attention core of the reference's own sqrt_block module
+    (model/custom_attention.py:183-227) on (B, T, H, D) CUDA views; T must be a
+    perfect square.  o: (B, T, H, D); glob: (B, H, G, G) fp32; summary:
+    (B, H, G, L) fp32 (both saved for the backward).
+    """
+    q, k, v = _prep(q, "q"), _prep(k, "k"), _prep(v, "v")
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError(f"q, k, v shapes differ: {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in _DTYPES:
+        raise TypeError(f"q, k, v must share a float32 or bfloat16 dtype, got "
+                        f"{q.dtype}, {k.dtype}, {v.dtype}")
+    B, T, H, D = q.shape
+    L = _refsem_check_T(T)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = q.device
+    o = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    glob = torch.empty((B, H, L, L), dtype=torch.float32, device=dev)
+    summary = torch.empty((B, H, L, L), dtype=torch.float32, device=dev)
+    ws = _refsem_workspace(dev, (B, T, H, D))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    st = _lib.strides_array(_strides(q), _strides(k), _strides(v), _strides(o))
+    rc = _lib.lib().sqb_refsem_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                   glob.data_ptr(), summary.data_ptr(), B, T, H, D, st,
+                                   _DTYPES[q.dtype], float(scale), ws.data_ptr(), ws.numel(),
+                                   stream)
+    _lib.check("sqb_refsem_fwd", rc)
+    return o, glob, summary
+
+
+def reference_backward(q, k, v, glob, summary, dout, scale=None):
+    """Reference-semantics backward -> (dq, dk, dv), each (B, T, H, D)."""
+    q, k, v, dout = _prep(q, "q"), _prep(k, "k"), _prep(v, "v"), _prep(dout, "dout")
+    if dout.dtype != q.dtype:
+        dout = dout.to(q.dtype)
+    B, T, H, D = q.shape
+    _refsem_check_T(T)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = q.device
+    dq = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    dk = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    dv = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    ws = _refsem_workspace(dev, (B, T, H, D))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    st = _lib.strides_array(*(_strides(t) for t in (q, k, v, dout, dq, dk, dv)))
+    rc = _lib.lib().sqb_refsem_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), dout.data_ptr(),
+                                   glob.contiguous().data_ptr(), summary.contiguous().data_ptr(),
+                                   dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, T, H, D, st,
+                                   _DTYPES[q.dtype], float(scale), ws.data_ptr(), ws.numel(),
+                                   stream)
+    _lib.check("sqb_refsem_bwd", rc)
+    return dq, dk, dv
+
+
+class _ReferenceAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, scale):
+        o, glob, summary = reference_forward(q, k, v, scale)
+        ctx.save_for_backward(q, k, v, glob, summary)
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, glob, summary = ctx.saved_tensors
+        dq, dk, dv = reference_backward(q, k, v, glob, summary, dout, ctx.scale)
+        return dq, dk, dv, None
+
+
+def reference_attention(q, k, v, scale=None):
+    """Differentiable reference-semantics attention on (B, T, H, D) CUDA views -> O."""
+    return _ReferenceAttention.apply(q, k, v, scale)

@@ -14,6 +14,13 @@ Fixtures written:
   which is exactly the sqrt-block operator's block 0.  The module's Wq/Wk/Wv
   are seeded random and c_proj is the identity, so the stored output is the
   attention core's.  Inputs are stored as float16 values (exact in float64).
+* ``refsem_T256.npz`` / ``refsem_T1024.npz`` - the reference module's full
+  attention core (all blocks, its own semantics: column-sum summaries, the G x G
+  summary softmax and the fixed-weight own block, custom_attention.py:183-225 and
+  _ScaledBlockCombine :82-135) and its autograd gradients, run in float64 with
+  its Wq/Wk/Wv replaced by modules returning seeded leaf tensors Q, K, V and
+  c_proj the identity, so the stored output and dQ/dK/dV are the core's.  They
+  pin oracle/refsem_oracle.py and the CUDA reference-semantics mode.
 * ``oracle_T200.npz`` - a frozen forward/backward of the oracle itself on a
   ragged case (T=200, b=16: 12 complete blocks and a partial block of 8), so
   any later change to the oracle shows up as a fixture mismatch.
@@ -65,6 +72,47 @@ def _reference_block0(ref_root, B, H, T, D, seed):
         y = mod(torch.from_numpy(x.astype(np.float64))).numpy()
     L = int(round(T ** 0.5))
     return x, w, y[:, :L, :], y
+
+
+def _reference_full(ref_root, B, H, T, D, seed):
+    """Output and dQ/dK/dV of the reference's attention core on seeded Q/K/V/dO."""
+    import torch
+
+    sys.path.insert(0, ref_root)
+    try:
+        from model.custom_attention import CustomAttention  # noqa: E402
+    finally:
+        sys.path.pop(0)
+
+    class Cfg:
+        n_embd = H * D
+        n_head = H
+        block_size = T
+        bias = False
+        dropout = 0.0
+
+    class Fixed(torch.nn.Module):
+        """Stands in for a projection: returns a given leaf tensor."""
+
+        def __init__(self, t):
+            super().__init__()
+            self.t = t
+
+        def forward(self, x):
+            return self.t
+
+    C = H * D
+    rng = np.random.default_rng(seed)
+    q, k, v, do = [rng.standard_normal((B, T, H, D)).astype(np.float16) for _ in range(4)]
+    mod = CustomAttention(Cfg()).double().eval()
+    leaves = [torch.from_numpy(a.astype(np.float64)).reshape(B, T, C).requires_grad_()
+              for a in (q, k, v)]
+    mod.Wq, mod.Wk, mod.Wv = (Fixed(t) for t in leaves)
+    mod.c_proj = torch.nn.Identity()
+    y = mod(torch.zeros(B, T, C, dtype=torch.float64))
+    y.backward(torch.from_numpy(do.astype(np.float64)).reshape(B, T, C))
+    grads = [t.grad.numpy().reshape(B, T, H, D) for t in leaves]
+    return q, k, v, do, y.detach().numpy().reshape(B, T, H, D), grads
 
 
 def main():
@@ -130,6 +178,22 @@ def main():
                               "n_embd": 64, "attention": "sqrt_block"}, "keys": keys}, f,
                   indent=1, sort_keys=True)
     print(f"wrote {path}")
+
+    from oracle import refsem_oracle as rso
+
+    for (B, H, T, D, seed) in [(2, 2, 256, 32, 4), (1, 1, 1024, 32, 5)]:
+        q, k, v, do, y, (dq, dk, dv) = _reference_full(args.reference, B, H, T, D, seed)
+        # (B, T, H, D) -> (B, H, T, D) for the oracle
+        t = lambda a: a.astype(np.float64).transpose(0, 2, 1, 3)  # noqa: E731
+        o_orc, _, _ = rso.fwd(t(q), t(k), t(v))
+        g_orc = rso.bwd(t(q), t(k), t(v), t(do))
+        err = max([np.abs(o_orc - t(y)).max()] +
+                  [np.abs(a - t(b)).max() for a, b in zip(g_orc, (dq, dk, dv))])
+        path = os.path.join(HERE, f"refsem_T{T}.npz")
+        np.savez_compressed(path, q=q, k=k, v=v, do=do, o=y.astype(np.float32),
+                            dq=dq.astype(np.float32), dk=dk.astype(np.float32),
+                            dv=dv.astype(np.float32))
+        print(f"wrote {path}: max|oracle - reference| = {err:.3e}")
 
     B, H, T, D, b = 1, 2, 200, 32, 16
     rng = np.random.default_rng(3)
