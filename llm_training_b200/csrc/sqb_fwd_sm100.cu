@@ -14,9 +14,10 @@
 //   O += P V             tcgen05.mma, A = P from TMEM (bf16), B = V smem
 // The online softmax spans both kinds of chunk, so in-block keys and
 // summaries share one softmax.  LSE (natural log) and O are written at the
-// end.  O leaves through a small per-warp transpose buffer (32 rows x 64
-// bytes) with coalesced global stores, so no operand buffer is held by the
-// epilogue and the next tile's K/V loads - and with them its pooling and the
+// end.  O leaves through a per-warp ring of three 1 KB store units (16 rows x
+// 32 columns), each handed to a TMA store as soon as it is written: the
+// softmax warps never wait on the global write path, and no operand buffer is
+// held, so the next tile's K/V loads - and with them its pooling and the
 // summary flags later tiles wait on - are never delayed by an O store.
 //
 // Summaries cross CTAs: tiles are handed out in ascending sequence order
@@ -44,8 +45,6 @@ struct FwdParams {
   __nv_bfloat16* kbar;
   __nv_bfloat16* vbar;
   float* lse;
-  __nv_bfloat16* o;
-  int64_t o_sb, o_st, o_sh;  // element strides of O (batch, token, head)
   uint32_t* ctrl;
   uint32_t* flags;
   int flags_stride;
@@ -61,9 +60,10 @@ struct FwdSmem {
   alignas(1024) uint8_t q[NQ][kTileBytes];
   alignas(1024) uint8_t k[NKV][kTileBytes];
   alignas(1024) uint8_t v[NKV][kTileBytes];
-  float red[4][2][D];
-  // per softmax warp: 32 rows x 32 columns of O (bf16), 16-byte chunks swizzled
-  alignas(16) uint8_t ostage[4][32 * 64];
+  float red[4][D];  // pooling: per-warp partial sums of one of K / V
+  // per softmax warp: a ring of three O store units, 16 rows x 32 columns bf16
+  // each, 16-byte chunks in the TMA 64-byte swizzle (chunk ^= (row / 2) % 4)
+  alignas(1024) uint8_t ostage[4][3][1024];
   uint64_t q_full[NQ], q_empty[NQ];
   uint64_t k_full[NKV], k_empty[NKV], v_full[NKV], v_empty[NKV];
   uint64_t s_full[NS], p_full[NS], s_free[NS], o_full, o_free;
@@ -98,7 +98,8 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 q) {
 template <int D, int NQ, int NKV, int NS, bool kSplit>
 __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kbar,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+               const __grid_constant__ CUtensorMap tm_kbar,
                const __grid_constant__ CUtensorMap tm_vbar, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   FwdSmem<D, NQ, NKV, NS>& sm = *reinterpret_cast<FwdSmem<D, NQ, NKV, NS>*>(
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     ptx::tma_prefetch_desc(&tm_q);
     ptx::tma_prefetch_desc(&tm_k);
     ptx::tma_prefetch_desc(&tm_v);
+    ptx::tma_prefetch_desc(&tm_o);
   }
   if (warp == 1) {
     ptx::tmem_alloc(&sm.tmem_base, kTmemCols);
@@ -316,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t o_addr = tmem + lane_off + NS * 128;
     int tc = 0, gc = 0;
+    int ucount = 0;  // O store units this warp has issued (ring position)
     while (true) {
       const int slot = tc % NQ;
       ptx::mbar_wait(&sm.q_full[slot], (tc / NQ) & 1, status, 0x30000000u | slot);
@@ -444,22 +447,24 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&sm.p_full[x]);
       }
-      // ---- epilogue: O / l -> bf16, 32 columns at a time through the warp's
-      // transpose buffer: each lane writes its row's 64 bytes, then reads 16
-      // bytes of row 8i + lane/4, so one store instruction covers 8 rows x 64
-      // contiguous bytes instead of 32 rows x 16 bytes.
+      // ---- epilogue: O / l -> bf16 into the warp's ring of store units, 32
+      // columns (two units of 16 rows) at a time, each unit stored by TMA as
+      // soon as it is written.  Each store is its own bulk group; before a
+      // piece's two units are rewritten, at most the previous piece's second
+      // store (in the third slot) may still be reading.
       ptx::mbar_wait(&sm.o_full, tc & 1, status, 0x33000000u);
       ptx::tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      uint8_t* ost = sm.ostage[quarter];
-      const int rsub = lane >> 2, csub = lane & 3;  // read-back: row in an 8-row group, chunk
-      const int64_t o_rows0 = (int64_t)t.n * p.o_sb + (int64_t)t.h * p.o_sh;
+      const int ug = lane >> 4, ur = lane & 15;  // this lane's unit (row group) and row in it
 #pragma unroll 1
       for (int pc = 0; pc < D / 32; ++pc) {
         uint32_t r0[32];
         ptx::tmem_ld32(o_addr + pc * 32, r0);
         ptx::tmem_wait_ld();
         ptx::reg_fence(r0);
+        if (lane == 0) ptx::tma_store_wait_read_1();
+        __syncwarp();
+        uint8_t* unit = sm.ostage[quarter][(ucount + ug) % 3];
 #pragma unroll
         for (int j8 = 0; j8 < 4; ++j8) {
           uint4 w;
@@ -471,20 +476,23 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
                                  __uint_as_float(r0[8 * j8 + 5]) * inv_l);
           w.w = ptx::pack_bf16x2(__uint_as_float(r0[8 * j8 + 6]) * inv_l,
                                  __uint_as_float(r0[8 * j8 + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(ost + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = w;
+          *reinterpret_cast<uint4*>(unit + ur * 64 + ((j8 ^ ((ur >> 1) & 3)) << 4)) = w;
         }
+        ptx::fence_proxy_async_smem();
         __syncwarp();
+        if (lane == 0) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = 8 * i + rsub;  // row of this warp's 32
-          const uint4 w =
-              *reinterpret_cast<const uint4*>(ost + r * 64 + ((csub ^ ((r >> 1) & 3)) << 4));
-          if (quarter * 32 + r < t.rows)
-            *reinterpret_cast<uint4*>(p.o + o_rows0 +
-                                      (int64_t)(t.r0 + quarter * 32 + r) * p.o_st + pc * 32 +
-                                      csub * 8) = w;
+          for (int g = 0; g < 2; ++g) {
+            // a row group past the tile's rows belongs to the next tile (or
+            // lies past T, where TMA clips the store)
+            const int row0 = quarter * 32 + g * 16;
+            if (row0 < t.rows)
+              ptx::tma_store_4d(&tm_o, sm.ostage[quarter][(ucount + g) % 3], pc * 32, t.h,
+                                t.r0 + row0, t.n);
+            ptx::tma_store_commit();
+          }
         }
-        __syncwarp();
+        ucount += 2;
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -493,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       gc += nch;
       ++tc;
     }
+    if (lane == 0) ptx::tma_store_wait_all();  // the O stores have completed
   } else {
     // ------------------------------------------------------------ pooling
     const int ptid = threadIdx.x - 192;  // 0..127
@@ -545,12 +554,12 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
               for (int j = 0; j < 8; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], 16);
               if ((ptid & 16) == 0 && cc < D / 8) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) sm.red[pw][kv][cc * 8 + j] = a[j];
+                for (int j = 0; j < 8; ++j) sm.red[pw][cc * 8 + j] = a[j];
               }
               ptx::named_barrier(2, 128);
               if (ptid < D) {
-                const float sum = sm.red[0][kv][ptid] + sm.red[1][kv][ptid] +
-                                  sm.red[2][kv][ptid] + sm.red[3][kv][ptid];
+                const float sum =
+                    sm.red[0][ptid] + sm.red[1][ptid] + sm.red[2][ptid] + sm.red[3][ptid];
                 dst[((size_t)t.bh * p.g.Gc + t.blk0 + lb) * D + ptid] =
                     __float2bfloat16_rn(sum * inv_b);
               }
@@ -577,19 +586,16 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
             acck[j] += __shfl_xor_sync(0xffffffffu, acck[j], 16);
             accv[j] += __shfl_xor_sync(0xffffffffu, accv[j], 16);
           }
-          if ((ptid & 16) == 0 && cc < D / 8) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              sm.red[pw][0][cc * 8 + j] = acck[j];
-              sm.red[pw][1][cc * 8 + j] = accv[j];
-            }
-          }
 #pragma unroll 1
           for (int kv = 0; kv < 2; ++kv) {
+            if ((ptid & 16) == 0 && cc < D / 8) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) sm.red[pw][cc * 8 + j] = kv == 0 ? acck[j] : accv[j];
+            }
             ptx::named_barrier(2, 128);
             if (ptid < D) {
-              const float sum = sm.red[0][kv][ptid] + sm.red[1][kv][ptid] +
-                                sm.red[2][kv][ptid] + sm.red[3][kv][ptid];
+              const float sum =
+                  sm.red[0][ptid] + sm.red[1][ptid] + sm.red[2][ptid] + sm.red[3][ptid];
               (kv == 0 ? p.kbar : p.vbar)[((size_t)t.bh * p.g.Gc + t.blk0) * D + ptid] =
                   __float2bfloat16_rn(sum * inv_b);
             }
@@ -636,8 +642,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
 }
 
 template <int D, int NQ, int NKV, int NS, bool kSplit>
-int launch(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, void* kbar,
-           void* vbar, uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
+int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
+           uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   FwdParams p;
   p.g.T = pr.T;
   p.g.b = pr.b;
@@ -652,10 +658,6 @@ int launch(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, vo
   p.kbar = reinterpret_cast<__nv_bfloat16*>(kbar);
   p.vbar = reinterpret_cast<__nv_bfloat16*>(vbar);
   p.lse = lse;
-  p.o = reinterpret_cast<__nv_bfloat16*>(o.ptr);
-  p.o_sb = o.sb;
-  p.o_st = o.st;
-  p.o_sh = o.sh;
   p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_fwd);
   p.flags_stride = wl.tiles_per_seq;
@@ -666,23 +668,22 @@ int launch(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, vo
     return SQB_ERR_LAUNCH;
   const int slots = num_sms * ctas_per_sm<NQ, NKV, NS>();
   const int grid = p.total_tiles < slots ? p.total_tiles : slots;
-  kern<<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kbar, tm.vbar, p);
+  kern<<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.kbar, tm.vbar, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 
 }  // namespace
 
-int launch_forward(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, void* kbar,
-                   void* vbar, uint8_t* ws, const WorkspaceLayout& wl, int num_sms,
-                   cudaStream_t stream) {
+int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
+                   uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   // single-buffered, two CTAs per SM (measured faster than one double-buffered CTA)
   const bool split = pr.b > 128;
   if (pr.D == 64)
-    return split ? launch<64, 1, 1, 1, true>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream)
-                 : launch<64, 1, 1, 1, false>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream);
+    return split ? launch<64, 1, 1, 1, true>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream)
+                 : launch<64, 1, 1, 1, false>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
   if (pr.D == 128)
-    return split ? launch<128, 1, 1, 1, true>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream)
-                 : launch<128, 1, 1, 1, false>(pr, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream);
+    return split ? launch<128, 1, 1, 1, true>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream)
+                 : launch<128, 1, 1, 1, false>(pr, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
   return SQB_ERR_UNSUPPORTED;
 }
 

@@ -73,6 +73,20 @@ bool encode_bthd(CUtensorMap* m, const Problem& p, const TensorView& t, int rows
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// (B, T, H, D) bf16 view as a store map with box {32, 1, 16, 1} (64 bytes x 16
+// rows) and the 64-byte swizzle: the forward's per-warp O store units.
+bool encode_bthd_store16(CUtensorMap* m, const Problem& p, const TensorView& t) {
+  const cuuint64_t dims[4] = {(cuuint64_t)p.D, (cuuint64_t)p.H, (cuuint64_t)p.T, (cuuint64_t)p.B};
+  const cuuint64_t strides[3] = {(cuuint64_t)t.sh * 2, (cuuint64_t)t.st * 2,
+                                 (cuuint64_t)t.sb * 2};
+  const cuuint32_t box[4] = {32, 1, 16, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.ptr, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // (B*H, Gc, D) contiguous bf16 summaries as {D, Gc, BH}, box {64, 128, 1}.
 bool encode_summaries(CUtensorMap* m, const Problem& p, const void* ptr) {
   const cuuint64_t dims[3] = {(cuuint64_t)p.D, (cuuint64_t)p.Gc, (cuuint64_t)p.B * p.H};
@@ -104,7 +118,8 @@ int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, Te
   if (!device_ok(&num_sms)) return SQB_ERR_DEVICE;
   const int R = sm100::tile_rows(p.b);
   sm100::TensorMaps tm;
-  if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) || !encode_bthd(&tm.v, p, v, R))
+  if (!encode_bthd(&tm.q, p, q, R) || !encode_bthd(&tm.k, p, k, R) ||
+      !encode_bthd(&tm.v, p, v, R) || !encode_bthd_store16(&tm.o, p, o))
     return SQB_ERR_CUDA;
   if (p.Gc > 0) {
     if (!encode_summaries(&tm.kbar, p, kbar) || !encode_summaries(&tm.vbar, p, vbar))
@@ -113,7 +128,7 @@ int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, Te
     tm.kbar = tm.k;  // never read: a sequence shorter than one block has no summaries
     tm.vbar = tm.v;
   }
-  return sm100::launch_forward(p, tm, o, lse, kbar, vbar, ws, wl, num_sms, stream);
+  return sm100::launch_forward(p, tm, lse, kbar, vbar, ws, wl, num_sms, stream);
 }
 
 int sm100_backward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,

@@ -47,11 +47,11 @@ inline int tiles_per_seq(int T, int b) {
 
 struct TensorMaps {
   CUtensorMap q, k, v, kbar, vbar;
+  CUtensorMap o;  // store map: box of 32 columns x 16 rows, 64-byte swizzle
 };
 
-int launch_forward(const Problem& pr, const TensorMaps& tm, TensorView o, float* lse, void* kbar,
-                   void* vbar, uint8_t* ws, const WorkspaceLayout& wl, int num_sms,
-                   cudaStream_t stream);
+int launch_forward(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void* vbar,
+                   uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream);
 
 struct BwdTensorMaps {
   CUtensorMap q, k, v, o, dout, dq, dk, dv, kbar, vbar;
