@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload attn-t4k|attn-t8k|attn-t16k|attn-t32k|attn-t64k|gpt2-small|
-                                gpt2-medium-8k]
+                                gpt2-medium-8k|refsem-cfg2]
 
 One step = one forward (sqb_fwd) and one backward (sqb_bwd) of the attention
 operator over the whole workload.  ``value`` is whole-job algorithmic HBM
@@ -12,6 +12,10 @@ over ranks, divided by the max-over-ranks device time).  Inputs (Q, K, V, dO:
 needed between steps.  Multi-GPU: one process per GPU under torchrun, every
 rank runs its own 16 heads (weak scaling; the (batch, head) units are
 independent, so there is no data-path collective).
+
+``--workload refsem-cfg2`` times the reference-semantics mode (the reference's
+own sqrt_block attention core, ``sqb_refsem_fwd`` / ``sqb_refsem_bwd``) at the
+B=8, H=12, T=1024, D=64 bf16 shape, with its float64 CPU oracle timed beside it.
 
 ``--impl reference`` times the CPU restatement of the operator (the
 reference repository has no implementation of it) on the host cores, on a
@@ -401,6 +405,69 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# reference-semantics mode: (B, H, T, D) of the cfg-2 shape (T a perfect square)
+REFSEM = {"refsem-cfg2": (8, 12, 1024, 64)}
+
+
+def run_refsem(args, world, rank, local):
+    """Reference-semantics mode (the reference's own attention core), fwd+bwd."""
+    from llm_training_b200.ops import read_status, reference_backward, reference_forward
+
+    Bq, Hq, Tq, Dq = REFSEM[args.workload]
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
+    host = [torch.randn(Bq, Tq, Hq, Dq, generator=g).to(torch.bfloat16) for _ in range(4)]
+    q, k, v, do = [x.to(dev) for x in host]
+
+    def step():
+        o, glob, summary = reference_forward(q, k, v)
+        reference_backward(q, k, v, glob, summary, do)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    # fwd reads Q, K, V and writes O; bwd reads Q, K, V, dO and writes dQ, dK, dV
+    step_bytes = 11 * Bq * Tq * Hq * Dq * 2
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import numpy as np
+
+        from oracle import refsem_oracle as rso
+
+        x = [h[:1, :, :1].float().numpy().transpose(0, 2, 1, 3).astype(np.float64) for h in host]
+        t0 = time.perf_counter()
+        rso.fwd(*x[:3])
+        rso.bwd(*x)
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(11 * Tq * Dq * 2 / dt / 1e9, 4), "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": f"1 of {Bq * Hq} (batch, head) units, float64 numpy "
+                                         f"oracle fwd+bwd, {dt * 1e3:.1f} ms"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "reference-semantics sqrt_block attn fwd+bwd GB/s (B=8 H=12 T=1024 D=64)",
+            "value": round(step_bytes * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded per rank",
+            "config": {"workload": args.workload, "B": Bq, "H": Hq, "T": Tq, "D": Dq,
+                       "mode": "reference semantics (CUDA-core kernels)",
+                       "parallelism": f"replicas x {world} ranks"},
+            "cpu_baseline": cpu, "gpu_launches": 7 * args.steps, "clocks": clocks.summary(),
+            "device_status": read_status(dev),
+        }), flush=True)
+
+
 TRAIN_WORKLOADS = {
     # name: (config factory kwargs, sequences per GPU, sequence length)
     "gpt2-small": ("small", 16, 1024),
@@ -479,7 +546,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--warmup-seconds", type=float, default=0.5,
                     help="keep warming up at least this long (clock sampler needs samples)")
-    ap.add_argument("--workload", choices=sorted(SWEEP) + sorted(TRAIN_WORKLOADS),
+    ap.add_argument("--workload", choices=sorted(SWEEP) + sorted(TRAIN_WORKLOADS) + sorted(REFSEM),
                     default="attn-t16k",
                     help="attn-t*: the attention op at that sweep length (attn-t16k is the "
                          "default); gpt2-*: a training step")
@@ -488,7 +555,16 @@ def main():
     T = SWEEP.get(args.workload, T)
     world, rank, local = init_dist()
     try:
-        if args.workload not in SWEEP:
+        if args.workload in REFSEM:
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable":
+                                      "the reference module runs only in the survey container; "
+                                      "its CPU oracle is timed in this workload's cpu_baseline"}),
+                          flush=True)
+            else:
+                run_refsem(args, world, rank, local)
+        elif args.workload not in SWEEP:
             if args.impl == "reference":
                 if rank == 0:
                     print(json.dumps({"impl": "reference", "unavailable":

@@ -122,3 +122,25 @@ def test_profiler_hooks_register():
           m.register_full_backward_hook(lambda *a: None)]
     for h in hs:
         h.remove()
+
+
+@pytest.mark.parametrize("bias", [False, True])
+def test_reference_semantics_plugin_is_a_drop_in(bias):
+    """``sqrt_block_reference`` (the reference's own math) registers, has the
+    reference module's parameters and no persistent buffers, and a GPT built with
+    it has the reference GPT's state-dict keys, so reference checkpoints load."""
+    from llm_training_b200.model.sqrt_block_reference_attention import (
+        ReferenceSqrtBlockAttention)
+
+    assert reg.get_attention("sqrt-block-reference") is ReferenceSqrtBlockAttention
+    d = json.load(open(os.path.join(GOLDEN, "ref_state_dict_keys.json")))
+    c = d["config"]
+    cfg = ModelConfig(block_size=c["block_size"], vocab_size=c["vocab_size"],
+                      n_layer=c["n_layer"], n_head=c["n_head"], n_embd=c["n_embd"], bias=bias,
+                      attention="sqrt_block_reference")
+    model = GPT(cfg)
+    assert {k: list(v.shape) for k, v in model.state_dict().items()} == d["keys"][f"bias={bias}"]
+    m = model.transformer.attn_blocks[0].attn
+    assert isinstance(m, ReferenceSqrtBlockAttention)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.randn(1, 16, c["n_embd"]))
