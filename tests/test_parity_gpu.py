@@ -232,3 +232,18 @@ def test_product_library_is_in_tree():
     path = os.path.realpath(_lib.lib()._name)
     assert path.endswith("libsqrtblock.so")
     assert os.path.dirname(os.path.dirname(path)).endswith("llm_training_b200")
+
+
+@pytest.mark.parametrize("block", [None, 128])
+def test_growing_scores_within_blocks_bf16(block):
+    """Key norms grow along each block (x1 -> x6), so a row's scores rise steeply
+    from its first keys to its last and its running max moves between chunks
+    (the forward rescales O).  Checked against the float64 oracle like any
+    bf16 case."""
+    B, H, T, D = 1, 2, 1024, 64
+    b = block or orc.default_block(T)
+    q, k, v, do = inputs(B, H, T, D, 11, torch.float32)
+    pos = (torch.arange(T, device=k.device) % b).float() / b
+    k = k * (1.0 + 5.0 * pos)[None, :, None, None]
+    q, k, v, do = (x.to(torch.bfloat16) for x in (q, k, v, do))
+    check(q, k, v, do, block, run(q, k, v, do, block, "tcgen05"), torch.bfloat16)
