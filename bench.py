@@ -559,8 +559,9 @@ def main():
             if args.impl == "reference":
                 if rank == 0:
                     print(json.dumps({"impl": "reference", "unavailable":
-                                      "the reference module runs only in the survey container; "
-                                      "its CPU oracle is timed in this workload's cpu_baseline"}),
+                                      "the reference checkout is not present where the "
+                                      "benchmark runs; the workload's cpu_baseline times its "
+                                      "CPU oracle"}),
                           flush=True)
             else:
                 run_refsem(args, world, rank, local)
