@@ -77,6 +77,7 @@ struct BwdSmem {
   // loaded here (the tile's O still occupies the V buffer until delta is done)
   alignas(1024) uint8_t ds[2 * kAtomBytes];
   float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
+  float dpart[2][128];   // delta = rowsum(dO * O): the two column halves' sums
   uint64_t ld_full, ld_empty, k_full, k_empty, v_full, v_empty, s_full, ps_full, g_full, g_free;
   uint64_t delta_done, stage_free;
   uint64_t red_done, pub_read, sums_ready, sgrad_free;
@@ -365,26 +366,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int blk_t = valid ? tq / p.g.b : 0;
       const int lim = valid ? min(blk_t, p.g.Gc) : 0;
       const float L = valid ? p.lse[(size_t)t.bh * p.g.T + tq] * kLog2e : 0.f;
-      // delta = rowsum(dO * O); O was loaded into the V buffer.  Both halves
-      // compute the full dot product (cheaper than exchanging halves).
-      float delta = 0.f;
+      // delta = rowsum(dO * O); O was loaded into the V buffer.  Each half sums
+      // its D/2 columns; the halves meet in shared memory.
+      float dhalf = 0.f;
       if (valid) {
 #pragma unroll 4
-        for (int cc = 0; cc < D / 8; ++cc) {
+        for (int cc = half * (D / 16); cc < (half + 1) * (D / 16); ++cc) {
           const uint32_t off = swz_offset(row, cc * 8);
           const uint4 a = *reinterpret_cast<const uint4*>(sm.v + off);
           const uint4 g = *reinterpret_cast<const uint4*>(sm.dout + off);
-          delta += bf16lo(a.x) * bf16lo(g.x) + bf16hi(a.x) * bf16hi(g.x) +
+          dhalf += bf16lo(a.x) * bf16lo(g.x) + bf16hi(a.x) * bf16hi(g.x) +
                    bf16lo(a.y) * bf16lo(g.y) + bf16hi(a.y) * bf16hi(g.y) +
                    bf16lo(a.z) * bf16lo(g.z) + bf16hi(a.z) * bf16hi(g.z) +
                    bf16lo(a.w) * bf16lo(g.w) + bf16hi(a.w) * bf16hi(g.w);
         }
       }
+      sm.dpart[half][row] = dhalf;
+      // the previous tile's dK staging (P buffer) has been read by its TMA
+      // store before this tile's P/dS are written (after the barrier)
+      if (gtid == 0 && tc > 0) ptx::tma_store_wait_read_all();
       // This tile's O (V buffer) has been consumed into delta: the first V
-      // chunk may be loaded.  The barrier also orders this tile's P/dS writes
-      // after gtid 0's wait for the previous tile's staging stores.
+      // chunk may be loaded.
       ptx::named_barrier(1, 256);
       if (gtid == 0) ptx::mbar_arrive(&sm.delta_done);
+      const float delta = sm.dpart[0][row] + sm.dpart[1][row];
 
       // P and dS of one chunk into smem (this half's 64 key columns; masked -> 0)
       auto softmax_grad = [&](int N, int vlo, int vhi) {
@@ -579,68 +584,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         // contributions to its keys (and re-zeroes them)
         const bool cross = kSplit && valid && t.sub + 1 < block_tiles(p.g, t.blk0);
         const size_t xr = ((size_t)t.bh * p.G + t.blk0) * p.xrows + t.sub * kTileRows + row;
-        const float* skrow = sm.sgrad[0][lb_t];
-        const float* svrow = sm.sgrad[1][lb_t];
+        // dV (kv = 1: TMEM S columns -> dS buffer) or dK (kv = 0: dP columns ->
+        // P buffer) of the tile's keys, plus (summary gradient of the key's
+        // block) / b and, for b > 128, the later sub-tiles' contributions
+        auto stage_grad = [&](int kv) {
+          const uint32_t tcol = kv ? kColS : kColDP;
+          const float* srow = sm.sgrad[kv][lb_t];
+          float* xrow = (kv ? p.dvx : p.dkx) + xr * D;
+          uint8_t* dst = kv ? sm.ds : sm.p;
 #pragma unroll 1
-        for (int pc = 0; pc < kHalfD / 16; ++pc) {
-          const int col0 = half * kHalfD + pc * 16;
-          uint32_t gv[16], gk[16];
-          ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
-          ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
-          ptx::tmem_wait_ld();
-          ptx::reg_fence(gv);
-          ptx::reg_fence(gk);
+          for (int pc = 0; pc < kHalfD / 16; ++pc) {
+            const int col0 = half * kHalfD + pc * 16;
+            uint32_t g[16];
+            ptx::tmem_ld16(tmem + lane_off + tcol + col0, g);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(g);
 #pragma unroll
-          for (int j8 = 0; j8 < 2; ++j8) {
-            float fk[8], fv[8];
+            for (int j8 = 0; j8 < 2; ++j8) {
+              float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              fk[e] = __uint_as_float(gk[8 * j8 + e]);
-              fv[e] = __uint_as_float(gv[8 * j8 + e]);
-            }
-            const int col = col0 + j8 * 8;
-            if (complete) {
-              const float4 k0 = *reinterpret_cast<const float4*>(skrow + col);
-              const float4 k1 = *reinterpret_cast<const float4*>(skrow + col + 4);
-              const float4 v0 = *reinterpret_cast<const float4*>(svrow + col);
-              const float4 v1 = *reinterpret_cast<const float4*>(svrow + col + 4);
-              fk[0] += k0.x; fk[1] += k0.y; fk[2] += k0.z; fk[3] += k0.w;
-              fk[4] += k1.x; fk[5] += k1.y; fk[6] += k1.z; fk[7] += k1.w;
-              fv[0] += v0.x; fv[1] += v0.y; fv[2] += v0.z; fv[3] += v0.w;
-              fv[4] += v1.x; fv[5] += v1.y; fv[6] += v1.z; fv[7] += v1.w;
-            }
-            if (cross) {
-              float4* xk = reinterpret_cast<float4*>(p.dkx + xr * D + col);
-              float4* xv = reinterpret_cast<float4*>(p.dvx + xr * D + col);
-              const float4 k0 = __ldcg(xk), k1 = __ldcg(xk + 1);
-              const float4 v0 = __ldcg(xv), v1 = __ldcg(xv + 1);
-              if (p.g.tpb > 2) {
-                const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-                __stcg(xk, z);
-                __stcg(xk + 1, z);
-                __stcg(xv, z);
-                __stcg(xv + 1, z);
+              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(g[8 * j8 + e]);
+              const int col = col0 + j8 * 8;
+              if (complete) {
+                const float4 s0 = *reinterpret_cast<const float4*>(srow + col);
+                const float4 s1 = *reinterpret_cast<const float4*>(srow + col + 4);
+                f[0] += s0.x; f[1] += s0.y; f[2] += s0.z; f[3] += s0.w;
+                f[4] += s1.x; f[5] += s1.y; f[6] += s1.z; f[7] += s1.w;
               }
-              fk[0] += k0.x; fk[1] += k0.y; fk[2] += k0.z; fk[3] += k0.w;
-              fk[4] += k1.x; fk[5] += k1.y; fk[6] += k1.z; fk[7] += k1.w;
-              fv[0] += v0.x; fv[1] += v0.y; fv[2] += v0.z; fv[3] += v0.w;
-              fv[4] += v1.x; fv[5] += v1.y; fv[6] += v1.z; fv[7] += v1.w;
+              if (cross) {
+                float4* x = reinterpret_cast<float4*>(xrow + col);
+                const float4 x0 = __ldcg(x), x1 = __ldcg(x + 1);
+                if (p.g.tpb > 2) {
+                  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+                  __stcg(x, z);
+                  __stcg(x + 1, z);
+                }
+                f[0] += x0.x; f[1] += x0.y; f[2] += x0.z; f[3] += x0.w;
+                f[4] += x1.x; f[5] += x1.y; f[6] += x1.z; f[7] += x1.w;
+              }
+              *reinterpret_cast<uint4*>(dst + swz_offset(row, col)) =
+                  make_uint4(ptx::pack_bf16x2(f[0], f[1]), ptx::pack_bf16x2(f[2], f[3]),
+                             ptx::pack_bf16x2(f[4], f[5]), ptx::pack_bf16x2(f[6], f[7]));
             }
-            const uint32_t off = swz_offset(row, col);
-            *reinterpret_cast<uint4*>(sm.p + off) =
-                make_uint4(ptx::pack_bf16x2(fk[0], fk[1]), ptx::pack_bf16x2(fk[2], fk[3]),
-                           ptx::pack_bf16x2(fk[4], fk[5]), ptx::pack_bf16x2(fk[6], fk[7]));
-            *reinterpret_cast<uint4*>(sm.ds + off) =
-                make_uint4(ptx::pack_bf16x2(fv[0], fv[1]), ptx::pack_bf16x2(fv[2], fv[3]),
-                           ptx::pack_bf16x2(fv[4], fv[5]), ptx::pack_bf16x2(fv[6], fv[7]));
           }
-        }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          ptx::mbar_arrive(&sm.g_free);
-          ptx::mbar_arrive(&sm.sgrad_free);
-        }
+        };
+        auto issue_stores = [&](const CUtensorMap* tm, const uint8_t* src) {
+#pragma unroll
+          for (int a = 0; a < kAtoms; ++a)
+            for (int r = 0; r < t.rows; r += p.store_rows)
+              ptx::tma_store_4d(tm, src + a * kAtomBytes + r * 128, a * 64, t.h, t.r0 + r, t.n);
+        };
+        // 1. dQ (K buffer) and dV (dS buffer), stored as one bulk group: once it
+        // has been read, the next tile's first K and V chunks load there
 #pragma unroll 1
         for (int pc = 0; pc < kHalfD / 16; ++pc) {
           const int col0 = half * kHalfD + pc * 16;
@@ -659,23 +654,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  __uint_as_float(gq[8 * j8 + 7])));
           }
         }
+        stage_grad(1);
         ptx::fence_proxy_async_smem();
         ptx::named_barrier(1, 256);
         if (gtid == 0) {
-#pragma unroll
-          for (int a = 0; a < kAtoms; ++a) {
-            for (int r = 0; r < t.rows; r += p.store_rows) {
-              const uint32_t off = a * kAtomBytes + r * 128;
-              ptx::tma_store_4d(&tm_dk, sm.p + off, a * 64, t.h, t.r0 + r, t.n);
-              ptx::tma_store_4d(&tm_dv, sm.ds + off, a * 64, t.h, t.r0 + r, t.n);
-              ptx::tma_store_4d(&tm_dq, sm.k + off, a * 64, t.h, t.r0 + r, t.n);
-            }
-          }
+          issue_stores(&tm_dq, sm.k);
+          issue_stores(&tm_dv, sm.ds);
           ptx::tma_store_commit();
-          // the staging buffers are rewritten only after this read completes:
-          // P/dS by the next tile's first chunk (after the barrier that
-          // follows its delta) and K by its first chunk load (stage_free)
-          ptx::tma_store_wait_read_all();
+        }
+        // 2. dK (P buffer), its own bulk group
+        stage_grad(0);
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::mbar_arrive(&sm.g_free);
+          ptx::mbar_arrive(&sm.sgrad_free);
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::named_barrier(1, 256);
+        if (gtid == 0) {
+          issue_stores(&tm_dk, sm.p);
+          ptx::tma_store_commit();
+          // the dQ / dV group has been read: the K and dS buffers may take
+          // the next tile's first chunk loads (stage_free).  The P buffer is
+          // rewritten only after the barrier that follows the next tile's
+          // delta, before which this thread waits for the dK read.
+          ptx::tma_store_wait_read_1();
           ptx::mbar_arrive(&sm.stage_free);
         }
         ++kc;
