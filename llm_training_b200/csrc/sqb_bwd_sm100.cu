@@ -91,8 +91,10 @@ constexpr int kThreads = 352;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// TMEM columns: S / dV chunk at 0, dP / dK chunk at 128, dQ at 256.
-constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
+// TMEM columns: S / dV chunk at 0, dP / dK chunk at 128, dQ at 256; the
+// tile's last chunk takes S / dV at 384, so its S is computed while the
+// previous chunk's gradients are still read out of columns 0-255.
+constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256, kColSLast = 384;
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
@@ -292,15 +294,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nch = t.nsc + t.nin;
         for (int c = 0; c < nch; ++c) {
           const int N = c < t.nsc ? sum_chunk(t, c).n16 : in_chunk<kSplit>(t, c - t.nsc).n;
+          // a later last chunk's S goes to free columns: only its dP waits for
+          // the previous chunk's gradients to be read (g_free)
+          const bool late_last = c > 0 && c == nch - 1;
+          const uint32_t col_s = c == nch - 1 ? kColSLast : kColS;
           ptx::mbar_wait(&sm.k_full, kc & 1, status, 0x61000000u);
-          if (kc > 0) ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
+          if (kc > 0 && !late_last)
+            ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
           ptx::tc_fence_after();
           const uint32_t idesc_s = ptx::idesc_bf16(128, N, false, false);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            ptx::mma_ss(tmem + kColS, desc_kmajor(q_s, kk), desc_kmajor(k_s, kk), idesc_s,
+            ptx::mma_ss(tmem + col_s, desc_kmajor(q_s, kk), desc_kmajor(k_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
           ptx::mbar_wait(&sm.v_full, kc & 1, status, 0x64000000u);
+          if (late_last) ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
           ptx::tc_fence_after();
           const uint32_t vc_s = (c == 0 && t.nsc > 0) ? ds_s : v_s;  // where this chunk's V is
 #pragma unroll
@@ -323,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           kk > 0 ? 1u : 0u);
           } else {
             for (int kk = 0; kk < kq; ++kk)  // dVc = P^T dO
-              ptx::mma_ss(tmem + kColS, desc_mnmajor(p_s, kk), desc_mnmajor(do_s, kk), idesc_dvdk,
+              ptx::mma_ss(tmem + col_s, desc_mnmajor(p_s, kk), desc_mnmajor(do_s, kk), idesc_dvdk,
                           kk > 0 ? 1u : 0u);
             for (int kk = 0; kk < kq; ++kk)  // dKc = dS^T Q
               ptx::mma_ss(tmem + kColDP, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
@@ -392,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float delta = sm.dpart[0][row] + sm.dpart[1][row];
 
       // P and dS of one chunk into smem (this half's 64 key columns; masked -> 0)
-      auto softmax_grad = [&](int N, int vlo, int vhi) {
+      auto softmax_grad = [&](int N, int vlo, int vhi, uint32_t col_s) {
         const bool any_col = vhi > vlo;
         const int wlo = __reduce_min_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
         const int whi = __reduce_max_sync(0xffffffffu, any_col ? vhi : 0);
@@ -409,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         auto load = [&](int pi, uint32_t (&sv)[16], uint32_t (&dp)[16]) {
           if (live(pi)) {
-            ptx::tmem_ld16(tmem + lane_off + kColS + col0(pi), sv);
+            ptx::tmem_ld16(tmem + lane_off + col_s + col0(pi), sv);
             ptx::tmem_ld16(tmem + lane_off + kColDP + col0(pi), dp);
           }
         };
@@ -542,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- summary chunks: add dKc / dVc to the summary accumulators
       for (int c = 0; c < t.nsc; ++c) {
         const SumChunk sc = sum_chunk(t, c);
-        softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w);
+        softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w, kColS);
         if constexpr (kTransposedSums) {
           drain_sums_t(sc);
         } else {
@@ -558,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // sub-tiles of the block and are added to the workspace accumulators
       // that those sub-tiles' epilogues read.
       for (int u = 0; u + 1 < t.nin; ++u) {
-        softmax_grad(kTileRows, 0, valid ? kTileRows : 0);
+        softmax_grad(kTileRows, 0, valid ? kTileRows : 0, kColS);
         const size_t xr = ((size_t)t.bh * p.G + t.blk0) * p.xrows + u * kTileRows + row;
         // with two sub-tiles per block (b <= 256) a key's cross contribution
         // has one writer: stored, and never re-zeroed (each launch rewrites it
@@ -571,7 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) ptx::mbar_arrive(&sm.red_done);
 
       // ---- the in-block chunk of the tile's own rows (causal)
-      softmax_grad(t.n_in, valid ? max(0, blk_t * p.g.b - t.r0) : 0, valid ? row + 1 : 0);
+      softmax_grad(t.n_in, valid ? max(0, blk_t * p.g.b - t.r0) : 0, valid ? row + 1 : 0,
+                   kColSLast);
       // the publisher has staged sum / b of the tile's complete blocks
       ptx::mbar_wait(&sm.sums_ready, tc & 1, status, 0x73000000u);
       // dQ (the tile's last MMA) has read dS: the dS buffer may take dV staging
@@ -588,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // P buffer) of the tile's keys, plus (summary gradient of the key's
         // block) / b and, for b > 128, the later sub-tiles' contributions
         auto stage_grad = [&](int kv) {
-          const uint32_t tcol = kv ? kColS : kColDP;
+          const uint32_t tcol = kv ? kColSLast : kColDP;
           const float* srow = sm.sgrad[kv][lb_t];
           float* xrow = (kv ? p.dvx : p.dkx) + xr * D;
           uint8_t* dst = kv ? sm.ds : sm.p;
