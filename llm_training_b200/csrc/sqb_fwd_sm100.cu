@@ -48,6 +48,8 @@ struct FwdParams {
   uint32_t* ctrl;
   uint32_t* flags;
   int flags_stride;
+  int G;       // blocks per sequence
+  float* part;  // b > 128: K / V column sums of a block's earlier sub-tiles
 };
 
 // Pipeline depths: NQ query-tile slots, NKV key/value chunk stages, NS score
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
                            t.r0, t.n);
       }
       for (int u = 0; u < t.nin; ++u) {
-        const InChunk ic = in_chunk<kSplit>(t, u);
+        const InChunk ic = in_chunk<kSplit>(t, in_order<kSplit>(t, u));
         const int st = kc % NKV;
         const uint32_t par = ((kc / NKV) & 1) ^ 1;
         ptx::mbar_wait(&sm.k_empty[st], par, status, 0x11000000u | st);
@@ -261,7 +263,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         const int nch = t.nin + t.nsc;
         const uint32_t q_saddr = ptx::smem_u32(sm.q[slot]);
         auto chunk_n = [&](int c) {
-          return c < t.nin ? in_chunk<kSplit>(t, c).n : sum_chunk(t, c - t.nin).n16;
+          return c < t.nin ? in_chunk<kSplit>(t, in_order<kSplit>(t, c)).n
+                           : sum_chunk(t, c - t.nin).n16;
         };
         auto issue_pv = [&](int c) {
           const int g = gc + c, x = g % NS, st = (kc + c) % NKV;
@@ -336,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         int N, vlo, vhi;  // MMA width and the valid column range [vlo, vhi)
         if (c < t.nin) {
           // in-block keys [k0, k0 + N): those of the row's block up to the row
-          const InChunk ic = in_chunk<kSplit>(t, c);
+          const InChunk ic = in_chunk<kSplit>(t, in_order<kSplit>(t, c));
           N = ic.n;
           vlo = valid ? max(0, blk_t * p.g.b - ic.k0) : 0;
           vhi = valid ? min(tq - ic.k0 + 1, N) : 0;
@@ -518,12 +521,14 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       const Tile t = make_tile<kSplit>(p.g, p.H, n / p.BH, n % p.BH);
       {
         // b <= 128: each complete block of the tile's single in-block chunk is
-        // pooled and written on its own.  b > 128: the last sub-tile of a
-        // complete block sees the whole block in its in-block chunks and
-        // accumulates it across them; the other sub-tiles only pass the
-        // chunks through.
+        // pooled and written on its own.  b > 128: every sub-tile of a complete
+        // block sums the keys of its own rows (its diagonal chunk, processed
+        // first); each but the last leaves its K / V column sums in the
+        // workspace before releasing its flag, and the last adds them to its
+        // own and writes the block's means.  Later chunks only pass through,
+        // so no block summary waits on the softmax of a tile's earlier chunks.
         constexpr bool split = kSplit;
-        const bool pool_split = split && t.blk0 < p.g.Gc && t.sub == p.g.tpb - 1;
+        const bool pool_own = split && t.blk0 < p.g.Gc;
         const int nb = split ? 0 : p.g.R / p.g.b;
         const int nfull = max(0, min(nb, p.g.Gc - t.blk0));
         float acck[8], accv[8];  // b > 128: this thread's column sums of K, V
@@ -531,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         for (int j = 0; j < 8; ++j) acck[j] = accv[j] = 0.f;
         for (int u = 0; u < t.nin; ++u) {
           const int st = kc % NKV;
-          const int urows = u == t.nin - 1 ? t.rows : kTileRows;
+          const bool own = u == 0;  // the tile's diagonal chunk (in_order)
           // K then V: each buffer is released as soon as its own sums are read,
           // so the next chunk's K load can start while V is still pooled.
 #pragma unroll 1
@@ -565,8 +570,8 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
               }
               ptx::named_barrier(2, 128);
             }
-            if (pool_split && cc < D / 8) {
-              for (int i = 0; i < urows / 8; ++i) {
+            if (pool_own && own && cc < D / 8) {
+              for (int i = 0; i < t.rows / 8; ++i) {
                 const uint4 w = *reinterpret_cast<const uint4*>(buf + swz_offset(rg + 8 * i, cc * 8));
                 if (kv == 0)
                   add_bf16x8(acck, w);
@@ -579,33 +584,44 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
               ptx::mbar_arrive(kv == 0 ? &sm.k_empty[st] : &sm.v_empty[st]);
           }
           ++kc;
-        }
-        if (pool_split) {
+          if (!own) continue;
+          if (pool_own) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            acck[j] += __shfl_xor_sync(0xffffffffu, acck[j], 16);
-            accv[j] += __shfl_xor_sync(0xffffffffu, accv[j], 16);
-          }
+            for (int j = 0; j < 8; ++j) {
+              acck[j] += __shfl_xor_sync(0xffffffffu, acck[j], 16);
+              accv[j] += __shfl_xor_sync(0xffffffffu, accv[j], 16);
+            }
+            const bool last = t.sub == p.g.tpb - 1;
+            float* part = p.part + ((size_t)t.bh * p.G + t.blk0) * (p.g.tpb - 1) * 2 * D;
+            // the block's earlier sub-tiles have left their sums (their flags)
+            if (last && pw == 0)
+              ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s - t.sub, t.s,
+                                    token, status, (uint32_t)n);
 #pragma unroll 1
-          for (int kv = 0; kv < 2; ++kv) {
-            if ((ptid & 16) == 0 && cc < D / 8) {
+            for (int kv = 0; kv < 2; ++kv) {
+              if ((ptid & 16) == 0 && cc < D / 8) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) sm.red[pw][cc * 8 + j] = kv == 0 ? acck[j] : accv[j];
+                for (int j = 0; j < 8; ++j) sm.red[pw][cc * 8 + j] = kv == 0 ? acck[j] : accv[j];
+              }
+              ptx::named_barrier(2, 128);
+              if (ptid < D) {
+                float sum = sm.red[0][ptid] + sm.red[1][ptid] + sm.red[2][ptid] + sm.red[3][ptid];
+                if (!last) {
+                  part[(t.sub * 2 + kv) * D + ptid] = sum;
+                } else {
+                  for (int v = 0; v < t.sub; ++v) sum += __ldcg(part + (v * 2 + kv) * D + ptid);
+                  (kv == 0 ? p.kbar : p.vbar)[((size_t)t.bh * p.g.Gc + t.blk0) * D + ptid] =
+                      __float2bfloat16_rn(sum * inv_b);
+                }
+              }
+              ptx::named_barrier(2, 128);
             }
-            ptx::named_barrier(2, 128);
-            if (ptid < D) {
-              const float sum =
-                  sm.red[0][ptid] + sm.red[1][ptid] + sm.red[2][ptid] + sm.red[3][ptid];
-              (kv == 0 ? p.kbar : p.vbar)[((size_t)t.bh * p.g.Gc + t.blk0) * D + ptid] =
-                  __float2bfloat16_rn(sum * inv_b);
-            }
-            ptx::named_barrier(2, 128);
           }
+          // The barriers above order every pooling thread's summary (or
+          // partial-sum) writes before this release store, which makes them
+          // visible to any CTA that acquires the flag.
+          if (ptid == 0) ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
         }
-        // The barriers above order every pooling thread's summary writes
-        // before this release store, which makes them visible to any CTA that
-        // acquires the flag.
-        if (ptid == 0) ptx::st_release_gpu(p.flags + (size_t)t.bh * p.flags_stride + t.s, token);
       }
       for (int c = 0; c < t.nsc; ++c) {
         if (ptid == 0) {
@@ -661,6 +677,8 @@ int launch(const Problem& pr, const TensorMaps& tm, float* lse, void* kbar, void
   p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_fwd);
   p.flags_stride = wl.tiles_per_seq;
+  p.G = pr.G;
+  p.part = reinterpret_cast<float*>(ws + wl.pool_part);
   auto kern = fwd_kernel<D, NQ, NKV, NS, kSplit>;
   const size_t smem = sizeof(FwdSmem<D, NQ, NKV, NS>) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=

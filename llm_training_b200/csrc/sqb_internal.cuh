@@ -40,6 +40,9 @@ struct WorkspaceLayout {
   // b > 128 only: uint32[B*H*G] count of a block's sub-tiles that have read
   // its summary-gradient sums (the last one re-zeroes them)
   size_t readers;
+  // b > 128 only: fp32[B*H*G*(tpb-1)*2*D], the forward's K and V column sums
+  // of each sub-tile but the last of a block, which adds them to its own
+  size_t pool_part;
   size_t total;
   int tiles_per_seq;  // upper bound on work tiles per (batch, head)
 };
@@ -100,6 +103,9 @@ inline WorkspaceLayout workspace_layout(int64_t B, int64_t T, int64_t H, int64_t
   off = align_up(off, 256);
   w.readers = off;
   off += b > 128 ? (size_t)BH * G * 4 : 0;
+  off = align_up(off, 256);
+  w.pool_part = off;
+  off += b > 128 ? (size_t)BH * G * ((b + 127) / 128 - 1) * 2 * D * 4 : 0;
   w.total = align_up(off, 256);
   return w;
 }

@@ -93,6 +93,16 @@ __device__ inline InChunk in_chunk(const Tile& t, int u) {
   return k;
 }
 
+// In-block chunk processed i-th.  For b > 128 a tile takes its own diagonal
+// chunk (the keys of its rows) first: those are the keys it pools, so they
+// load at once and the block's summary does not wait on the softmax of the
+// tile's earlier chunks (whose V loads follow the previous chunk's PV).
+template <bool kSplit>
+__device__ inline int in_order(const Tile& t, int i) {
+  if constexpr (!kSplit) return i;
+  return i == 0 ? t.nin - 1 : i - 1;
+}
+
 // Tile (sequence index) whose pooling publishes summary j.
 template <bool kSplit>
 __device__ inline int summary_tile(const Geometry& g, int j) {
