@@ -375,11 +375,18 @@ def run_ours(args, world, rank, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
+        # one head of the workload per sample, repeated for ~10 s of CPU work
+        # (median sample; the first, untimed, warms the thread pool)
         heads = 1
-        dt, threads = cpu_sample_time(heads, 1)
+        _, threads = cpu_sample_time(heads, 1)
+        samples, t_end = [], time.perf_counter() + 10.0
+        while time.perf_counter() < t_end and len(samples) < 1000:
+            samples.append(cpu_sample_time(heads, 1)[0])
+        dt = statistics.median(samples)
         cpu = {"value": round(algorithmic_bytes(B, heads, T, D) / dt / 1e9, 3), "unit": "GB/s",
                "cores": threads, "kind": "port",
-               "sample": f"{heads} of {H} heads, fp32 torch fwd+bwd, {dt * 1e3:.0f} ms"}
+               "sample": f"{heads} of {H} heads, fp32 torch fwd+bwd, median of {len(samples)} "
+                         f"samples ({sum(samples):.1f} s; {dt * 1e3:.0f} ms each)"}
 
     if rank == 0:
         line = {
