@@ -331,7 +331,7 @@ def run_ours(args, world, rank, local):
             in_ready[i].record(s_in)
             stream.wait_event(in_ready[i])
             qd, kd, vd = (x.detach().requires_grad_(True) for x in buf[:3])
-            o = sqrt_block_attention(qd, kd, vd, block, None, "auto")
+            o = sqrt_block_attention(qd, kd, vd, block, None, args.kernels)  # as timed above
             o.backward(buf[3])
             res = (o.detach(), qd.grad, kd.grad, vd.grad)
             done[i].record(stream)
