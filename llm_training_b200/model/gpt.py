@@ -15,6 +15,7 @@ import math
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from .attention_registry import build_attention
 
@@ -85,7 +86,29 @@ class GPT(nn.Module):
         elif isinstance(module, nn.Embedding):
             torch.nn.init.normal_(module.weight, mean=0.0, std=0.02)
 
-    def forward(self, idx):
+    # vocabulary rows are padded to this multiple in the logits GEMM (pad_vocab)
+    VOCAB_ALIGN = 64
+
+    def _vocab_pad_bias(self, device, dtype):
+        """(Vp,): 0 for the real vocabulary, -inf for the padding (not a
+        parameter and not in the state dict)."""
+        V = self.config.vocab_size
+        Vp = -(-V // self.VOCAB_ALIGN) * self.VOCAB_ALIGN
+        bias = getattr(self, "_pad_bias", None)
+        if bias is None or bias.device != device or bias.dtype != dtype or bias.numel() != Vp:
+            bias = torch.zeros(Vp, device=device, dtype=dtype)
+            bias[V:] = float("-inf")
+            self.register_buffer("_pad_bias", bias, persistent=False)
+        return bias
+
+    def forward(self, idx, pad_vocab=False):
+        """Logits (B, T, vocab).  With ``pad_vocab`` the logits are (B, T, Vp),
+        Vp = vocab rounded up to a multiple of 64: the tied weight is zero-padded
+        for the GEMM and the padded columns get -inf, so they take no probability
+        and no gradient and a cross-entropy over them equals the unpadded one.
+        The padding keeps every GEMM operand's leading dimension 16-byte aligned
+        (vocab 50257 is odd, which sends these GEMMs to unaligned kernels several
+        times slower); the parameters are unchanged."""
         b, t = idx.size()
         assert t <= self.config.block_size, (
             f"Cannot forward sequence of length {t}, block size is only {self.config.block_size}")
@@ -93,4 +116,10 @@ class GPT(nn.Module):
         x = self.transformer.drop(self.transformer.wte(idx) + self.transformer.wpe(pos))
         for block in self.transformer.attn_blocks:
             x = block(x)
-        return self.lm_head(self.transformer.ln_(x))
+        h = self.transformer.ln_(x)
+        V = self.config.vocab_size
+        if not pad_vocab or V % self.VOCAB_ALIGN == 0:
+            return self.lm_head(h)
+        bias = self._vocab_pad_bias(h.device, self.lm_head.weight.dtype)
+        weight = F.pad(self.lm_head.weight, (0, 0, 0, bias.numel() - V))
+        return F.linear(h, weight, bias)

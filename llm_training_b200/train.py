@@ -22,7 +22,8 @@ from .model.gpt import GPT
 
 
 def calculate_loss(logits, targets):
-    """Next-token cross-entropy over (B*T, vocab)."""
+    """Next-token cross-entropy over (B*T, vocab) (or over the padded vocabulary
+    of ``GPT.forward(pad_vocab=True)``, whose extra columns are -inf)."""
     return F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
 
 
@@ -70,7 +71,7 @@ class Trainer:
         self.optimizer.zero_grad(set_to_none=True)
         with torch.autocast(device_type=self.device.type, dtype=torch.bfloat16,
                             enabled=self.autocast):
-            logits = self.model(x)
+            logits = self.model(x, pad_vocab=True)
             loss = calculate_loss(logits, y)
         loss.backward()
         norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), 1.0)

@@ -94,3 +94,30 @@ def test_gpu_training_step_with_sqrt_block_attention():
         loss, norm = tr.step(x, y)
     assert torch.isfinite(loss) and torch.isfinite(norm)
     assert float(loss) < first - 0.5
+
+
+def test_padded_vocab_logits_give_the_same_loss_and_gradients():
+    """The lm_head GEMM over a vocabulary padded to a multiple of 64 (-inf in the
+    padded columns) is the unpadded cross-entropy, value and gradients."""
+    from llm_training_b200.train import calculate_loss
+
+    torch.manual_seed(0)
+    cfg = tiny(vocab_size=97)
+    m = GPT(cfg).double()
+    gen = torch.Generator().manual_seed(1)
+    x, y = synthetic_batch(gen, 3, 16, 97, torch.device("cpu"))
+    losses, grads = [], []
+    for pad in (False, True):
+        m.zero_grad(set_to_none=True)
+        logits = m(x, pad_vocab=pad)
+        assert logits.shape[-1] == (128 if pad else 97)
+        loss = calculate_loss(logits, y)
+        loss.backward()
+        losses.append(loss.detach())
+        grads.append({n: p.grad.clone() for n, p in m.named_parameters()})
+    assert torch.allclose(losses[0], losses[1], rtol=1e-12, atol=1e-12)
+    for n in grads[0]:
+        assert torch.allclose(grads[0][n], grads[1][n], rtol=1e-10, atol=1e-12), n
+    # the padding is compute-only: the parameters and state-dict keys are unchanged
+    assert "_pad_bias" not in m.state_dict()
+    assert m.lm_head.weight.shape[0] == 97
