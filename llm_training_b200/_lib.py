@@ -64,6 +64,17 @@ class SqrtBlockError(RuntimeError):
         self.code = code
 
 
+# Training-caller helpers (include/sqb_train.h), bound on the same library.
+TRAIN_SIGNATURES = {
+    "sqb_xent_fwd": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p, _c_i64, _c_i64, _c_i64, ctypes.c_int,
+                                    ctypes.c_void_p]),
+    "sqb_xent_bwd": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_void_p, _c_i64, _c_i64, _c_i64,
+                                    ctypes.c_int, ctypes.c_void_p]),
+}
+
+
 def library_path() -> str:
     return os.environ.get("SQB_LIBRARY", LIBPATH)
 
@@ -81,7 +92,7 @@ def lib() -> ctypes.CDLL:
                     f"sqrt-block CUDA library not found at {path}; build it with "
                     "`python -m llm_training_b200.build` (there is no CPU fallback)")
             handle = ctypes.CDLL(path)
-            for name, (res, args) in SIGNATURES.items():
+            for name, (res, args) in {**SIGNATURES, **TRAIN_SIGNATURES}.items():
                 fn = getattr(handle, name)
                 fn.restype = res
                 fn.argtypes = args

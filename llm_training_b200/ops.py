@@ -17,7 +17,8 @@ import torch
 from . import _lib
 
 __all__ = ["sqrt_block_attention", "sqrt_block_forward", "sqrt_block_backward", "read_status",
-           "block_geometry", "reference_attention", "reference_forward", "reference_backward"]
+           "block_geometry", "reference_attention", "reference_forward", "reference_backward",
+           "cross_entropy"]
 
 _DTYPES = {torch.float32: _lib.SQB_F32, torch.bfloat16: _lib.SQB_BF16}
 
@@ -282,3 +283,53 @@ class _ReferenceAttention(torch.autograd.Function):
 def reference_attention(q, k, v, scale=None):
     """Differentiable reference-semantics attention on (B, T, H, D) CUDA views -> O."""
     return _ReferenceAttention.apply(q, k, v, scale)
+
+
+# ---- training caller: fused token cross-entropy (include/sqb_train.h) ------------
+
+
+class _CrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, targets):
+        V = logits.shape[-1]
+        x = logits.reshape(-1, V)
+        if x.stride(-1) != 1 or x.stride(0) < V:
+            x = x.contiguous()
+        t = targets.reshape(-1).to(torch.int64).contiguous()
+        if x.dtype not in _DTYPES or not x.is_cuda or t.numel() != x.shape[0]:
+            raise ValueError("cross_entropy: CUDA float32/bfloat16 logits (..., V) and one "
+                             "target per row")
+        N = x.shape[0]
+        loss = torch.empty(N, dtype=torch.float32, device=x.device)
+        lse = torch.empty(N, dtype=torch.float32, device=x.device)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check("sqb_xent_fwd", _lib.lib().sqb_xent_fwd(
+            x.data_ptr(), t.data_ptr(), loss.data_ptr(), lse.data_ptr(), N, V, x.stride(0),
+            _DTYPES[x.dtype], stream))
+        counted = (t >= 0).sum().to(torch.float32)
+        ctx.save_for_backward(x, t, lse, counted)
+        ctx.shape = logits.shape
+        return loss.sum() / counted
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, t, lse, counted = ctx.saved_tensors
+        scale = (grad.to(torch.float32) / counted).reshape(1).contiguous()
+        N, V = x.shape
+        ld = x.stride(0)
+        # the kernel writes whole rows of the logits' pitch (zeros past V): a full
+        # (N, ld) buffer, of which the first V columns are the gradient
+        dbuf = torch.empty(N, ld, dtype=x.dtype, device=x.device)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check("sqb_xent_bwd", _lib.lib().sqb_xent_bwd(
+            x.data_ptr(), t.data_ptr(), lse.data_ptr(), scale.data_ptr(), dbuf.data_ptr(), N, V,
+            ld, _DTYPES[x.dtype], stream))
+        return dbuf[:, :V].reshape(ctx.shape), None
+
+
+def cross_entropy(logits, targets):
+    """Mean next-token cross-entropy of CUDA logits (..., V) against integer targets
+    (negative = ignored), as ``F.cross_entropy`` computes it (fp32 math, mean over
+    the counted tokens), fused: the logits are read once forward and the gradient
+    written once backward, in the logits' dtype."""
+    return _CrossEntropy.apply(logits, targets)

@@ -23,7 +23,14 @@ from .model.gpt import GPT
 
 def calculate_loss(logits, targets):
     """Next-token cross-entropy over (B*T, vocab) (or over the padded vocabulary
-    of ``GPT.forward(pad_vocab=True)``, whose extra columns are -inf)."""
+    of ``GPT.forward(pad_vocab=True)``, whose extra columns are -inf).  On CUDA
+    the library's fused cross-entropy computes it (the same fp32 math as the
+    autocast ``F.cross_entropy`` of the reference, without its fp32 copies of
+    the logits); on CPU ``F.cross_entropy``."""
+    if logits.is_cuda:
+        from .ops import cross_entropy
+
+        return cross_entropy(logits, targets)
     return F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
 
 
