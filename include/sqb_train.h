@@ -7,7 +7,8 @@
  * gradient once in the logits' dtype.  It computes what the reference's
  * calculate_loss (training_utils.py:8-17: F.cross_entropy over the flattened
  * logits under bf16 autocast, fp32 softmax math) computes, per token; the mean
- * over the non-ignored tokens is taken by the caller.
+ * over the non-ignored tokens is taken by the caller.  And a LayerNorm (last
+ * entry points) with one warp per row and a fixed-order weight gradient.
  *
  * Conventions as in sqrtblock.h: caller-owned device pointers, asynchronous on
  * `stream` (a cudaStream_t; NULL = legacy default stream), return SQB_OK or an
@@ -40,6 +41,28 @@ int sqb_xent_fwd(const void* logits, const int64_t* targets, float* loss, float*
  * the number of counted tokens), read there so the host never waits. */
 int sqb_xent_bwd(const void* logits, const int64_t* targets, const float* lse, const float* scale,
                  void* dlogits, int64_t N, int64_t V, int64_t ld, int dtype, void* stream);
+
+/* LayerNorm over the last dimension of N contiguous fp32 rows of C (C a
+ * multiple of 128, at most 1024; else SQB_ERR_UNSUPPORTED):
+ *   y = (x - mean) / sqrt(var + eps) * weight + bias   (var biased; bias may be NULL),
+ * as torch.nn.LayerNorm computes it (the reference's LayerNorm module,
+ * model/layer_norm.py:4-13).  y has y_dtype: fp32, or bf16 - what a bf16
+ * autocast consumer of an fp32 LayerNorm would cast it to.  mean and rstd
+ * (1 / sqrt(var + eps)) are fp32 arrays of N for the backward.  x, weight,
+ * bias and y 16-byte aligned (else SQB_ERR_ALIGN). */
+int sqb_layernorm_fwd(const float* x, const float* weight, const float* bias, void* y, int y_dtype,
+                      float* mean, float* rstd, int64_t N, int64_t C, float eps, void* stream);
+
+/* Scratch bytes sqb_layernorm_bwd needs for N rows of C. */
+size_t sqb_layernorm_workspace_bytes(int64_t N, int64_t C);
+
+/* Backward: dx (fp32, N x C) from dy (dy_dtype) and the forward's x, mean and
+ * rstd; dweight and, unless dbias is NULL, dbias (fp32, C) are overwritten with
+ * their column sums, added in a fixed order (bit-reproducible). */
+int sqb_layernorm_bwd(const void* dy, int dy_dtype, const float* x, const float* weight,
+                      const float* mean, const float* rstd, float* dx, float* dweight,
+                      float* dbias, void* workspace, size_t ws_bytes, int64_t N, int64_t C,
+                      void* stream);
 
 #ifdef __cplusplus
 }

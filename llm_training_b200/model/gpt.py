@@ -28,6 +28,17 @@ class LayerNorm(nn.Module):
             self.ln.register_parameter("bias", None)
 
     def forward(self, x):
+        # CUDA fp32 rows (the residual stream): the library's fused LayerNorm,
+        # fp32 math as nn.LayerNorm under autocast, its output written directly
+        # in the autocast dtype that every consumer here (a Linear) casts it to
+        from ..ops import layer_norm, layer_norm_supported
+
+        if layer_norm_supported(x, self.ln.weight):
+            out = torch.float32
+            if torch.is_autocast_enabled("cuda"):
+                out = torch.get_autocast_dtype("cuda")
+            if out in (torch.float32, torch.bfloat16):
+                return layer_norm(x, self.ln.weight, self.ln.bias, self.ln.eps, out)
         return self.ln(x)
 
 

@@ -18,7 +18,7 @@ from . import _lib
 
 __all__ = ["sqrt_block_attention", "sqrt_block_forward", "sqrt_block_backward", "read_status",
            "block_geometry", "reference_attention", "reference_forward", "reference_backward",
-           "cross_entropy"]
+           "cross_entropy", "layer_norm", "layer_norm_supported"]
 
 _DTYPES = {torch.float32: _lib.SQB_F32, torch.bfloat16: _lib.SQB_BF16}
 
@@ -333,3 +333,62 @@ def cross_entropy(logits, targets):
     the counted tokens), fused: the logits are read once forward and the gradient
     written once backward, in the logits' dtype."""
     return _CrossEntropy.apply(logits, targets)
+
+
+# ---- training caller: fused LayerNorm (include/sqb_train.h) -----------------------
+
+
+def layer_norm_supported(x, weight) -> bool:
+    """The library's LayerNorm takes CUDA fp32 rows of C = 128k <= 1024 with an fp32
+    weight (the GPT caller's residual stream); other inputs use ``F.layer_norm``."""
+    C = x.shape[-1]
+    return (x.is_cuda and x.dtype == torch.float32 and weight is not None
+            and weight.dtype == torch.float32 and C % 128 == 0 and C <= 1024)
+
+
+class _LayerNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps, out_dtype):
+        C = x.shape[-1]
+        x2 = x.reshape(-1, C).contiguous()
+        N = x2.shape[0]
+        y = torch.empty((N, C), dtype=out_dtype, device=x.device)
+        mean = torch.empty(N, dtype=torch.float32, device=x.device)
+        rstd = torch.empty(N, dtype=torch.float32, device=x.device)
+        w = weight.contiguous()
+        b = bias.contiguous() if bias is not None else None
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check("sqb_layernorm_fwd", _lib.lib().sqb_layernorm_fwd(
+            x2.data_ptr(), w.data_ptr(), b.data_ptr() if b is not None else None, y.data_ptr(),
+            _DTYPES[out_dtype], mean.data_ptr(), rstd.data_ptr(), N, C, float(eps), stream))
+        ctx.save_for_backward(x2, w, mean, rstd)
+        ctx.has_bias = b is not None
+        ctx.shape = x.shape
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, mean, rstd = ctx.saved_tensors
+        N, C = x2.shape
+        dy2 = dy.reshape(N, C)
+        if dy2.dtype not in _DTYPES:
+            dy2 = dy2.float()
+        dy2 = dy2.contiguous()
+        dx = torch.empty((N, C), dtype=torch.float32, device=x2.device)
+        dw = torch.empty(C, dtype=torch.float32, device=x2.device)
+        db = torch.empty(C, dtype=torch.float32, device=x2.device) if ctx.has_bias else None
+        wsb = _lib.lib().sqb_layernorm_workspace_bytes(N, C)
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=x2.device)
+        stream = torch.cuda.current_stream(x2.device).cuda_stream
+        _lib.check("sqb_layernorm_bwd", _lib.lib().sqb_layernorm_bwd(
+            dy2.data_ptr(), _DTYPES[dy2.dtype], x2.data_ptr(), w.data_ptr(), mean.data_ptr(),
+            rstd.data_ptr(), dx.data_ptr(), dw.data_ptr(),
+            db.data_ptr() if db is not None else None, ws.data_ptr(), wsb, N, C, stream))
+        return dx.view(ctx.shape), dw, db, None, None
+
+
+def layer_norm(x, weight, bias=None, eps=1e-5, out_dtype=torch.float32):
+    """LayerNorm over the last dimension of CUDA fp32 ``x`` (see
+    ``layer_norm_supported``), fp32 math; the output in ``out_dtype`` (fp32, or
+    bf16 for a bf16 autocast consumer, which would cast it to that anyway)."""
+    return _LayerNorm.apply(x, weight, bias, eps, out_dtype)
