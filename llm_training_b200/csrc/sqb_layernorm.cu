@@ -164,13 +164,25 @@ __global__ void __launch_bounds__(kThreads, VPL * (kBias ? 3 : 2) <= 12 ? 2 : 1)
   }
 }
 
-// out[c] = sum over the `rows` partial rows of column c.
-__global__ void colsum_kernel(const float* part, float* out, int rows, int C) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
+// out[c] = sum over the `rows` partial rows of column c: a CTA of 8 x 32 threads
+// takes 32 columns, thread (g, j) sums rows g, g + 8, ... of column j and the
+// eight group sums are added in shared memory (a fixed order).
+__global__ void __launch_bounds__(256) colsum_kernel(const float* part, float* out, int rows,
+                                                     int C) {
+  __shared__ float red[8][33];
+  const int j = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + j;
   float t = 0.f;
-  for (int r = 0; r < rows; ++r) t += part[(int64_t)r * C + c];
-  out[c] = t;
+  if (c < C)
+    for (int r = grp; r < rows; r += 8) t += part[(int64_t)r * C + c];
+  red[grp][j] = t;
+  __syncthreads();
+  if (grp == 0 && c < C) {
+    float u = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) u += red[i][j];
+    out[c] = u;
+  }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -215,8 +227,8 @@ int launch_bwd(const void* dy, int dy_dtype, const float* x, const float* w, con
   else
     bwd_kernel<VPL, float, false><<<rows, kThreads, 0, s>>>(dyf, x, w, mean, rstd, dx, part_w,
                                                              part_b, N);
-  colsum_kernel<<<(C + 255) / 256, 256, 0, s>>>(part_w, dw, rows, C);
-  if (db) colsum_kernel<<<(C + 255) / 256, 256, 0, s>>>(part_b, db, rows, C);
+  colsum_kernel<<<(C + 31) / 32, 256, 0, s>>>(part_w, dw, rows, C);
+  if (db) colsum_kernel<<<(C + 31) / 32, 256, 0, s>>>(part_b, db, rows, C);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 
