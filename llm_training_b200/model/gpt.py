@@ -17,6 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..ops import layer_norm, layer_norm_supported
 from .attention_registry import build_attention
 
 
@@ -31,8 +32,6 @@ class LayerNorm(nn.Module):
         # CUDA fp32 rows (the residual stream): the library's fused LayerNorm,
         # fp32 math as nn.LayerNorm under autocast, its output written directly
         # in the autocast dtype that every consumer here (a Linear) casts it to
-        from ..ops import layer_norm, layer_norm_supported
-
         if layer_norm_supported(x, self.ln.weight):
             out = torch.float32
             if torch.is_autocast_enabled("cuda"):

@@ -19,6 +19,7 @@ import torch
 import torch.nn.functional as F
 
 from .model.gpt import GPT
+from .ops import cross_entropy
 
 
 def calculate_loss(logits, targets):
@@ -28,8 +29,6 @@ def calculate_loss(logits, targets):
     autocast ``F.cross_entropy`` of the reference, without its fp32 copies of
     the logits); on CPU ``F.cross_entropy``."""
     if logits.is_cuda:
-        from .ops import cross_entropy
-
         return cross_entropy(logits, targets)
     return F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
 
