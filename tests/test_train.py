@@ -121,3 +121,46 @@ def test_padded_vocab_logits_give_the_same_loss_and_gradients():
     # the padding is compute-only: the parameters and state-dict keys are unchanged
     assert "_pad_bias" not in m.state_dict()
     assert m.lm_head.weight.shape[0] == 97
+
+
+@pytest.mark.gpu
+def test_gpu_fused_caller_ops_match_torch_ops_end_to_end(monkeypatch):
+    """One autocast step of a small GPT: the fused LayerNorm, the fused
+    cross-entropy and the padded-vocabulary logits give the loss and gradients
+    of the same model on nn.LayerNorm, F.cross_entropy and unpadded logits."""
+    import torch.nn.functional as F
+
+    import llm_training_b200.model.gpt as gpt_mod
+
+    cfg = tiny(attention="sqrt_block", block_size=256, n_embd=256, n_head=4, vocab_size=1001)
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    m = GPT(cfg).to(dev)
+    gen = torch.Generator().manual_seed(3)
+    x, y = synthetic_batch(gen, 4, 256, 1001, dev)
+
+    def run(fused):
+        m.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            if fused:
+                from llm_training_b200.train import calculate_loss
+
+                loss = calculate_loss(m(x, pad_vocab=True), y)
+            else:
+                logits = m(x)
+                loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), y.reshape(-1))
+        loss.backward()
+        return loss.detach().float(), {n: p.grad.float().clone() for n, p in m.named_parameters()}
+
+    l_fused, g_fused = run(True)
+    with monkeypatch.context() as mp_:
+        mp_.setattr(gpt_mod, "layer_norm_supported", lambda *a: False)
+        l_ref, g_ref = run(False)
+    # the same values reach every bf16 GEMM; the LayerNorm statistics are summed
+    # in a different order, which bf16 rounding can amplify by an ulp here and there
+    torch.testing.assert_close(l_fused, l_ref, rtol=2e-3, atol=2e-3)
+    for n in g_ref:
+        a, b = g_fused[n].flatten(), g_ref[n].flatten()
+        cos = float(torch.dot(a, b) / (a.norm() * b.norm() + 1e-30))
+        assert cos > 0.999, (n, cos)
+        assert float((a.norm() - b.norm()).abs() / (b.norm() + 1e-30)) < 1e-2, n
