@@ -160,24 +160,30 @@ def make_inputs(seed, rank, device, dtype=torch.bfloat16, H_=H):
     return [torch.randn(B, T, H_, D, generator=g).to(dtype) for _ in range(4)]
 
 
-def cpu_sample_time(heads=1, reps=1):
+def cpu_samples(heads=1, reps=1, seconds=0.0):
     """Time the oracle port (fp32 torch, all host threads) on `heads` heads of
-    the workload, forward+backward; returns (seconds per sample, threads)."""
+    the workload, forward+backward, `reps` times and then until the timed work
+    adds up to `seconds`; returns (list of seconds per sample, threads)."""
     from oracle.torch_port import sqrt_block_attention_ref
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(0)
     q, k, v, do = [torch.randn(1, heads, T, D, generator=g) for _ in range(4)]
-    best = None
-    for _ in range(reps):
+    times = []
+    while len(times) < reps or (sum(times) < seconds and len(times) < 5000):
         qs, ks, vs = [x.clone().requires_grad_(True) for x in (q, k, v)]
         t0 = time.perf_counter()
         o, _ = sqrt_block_attention_ref(qs, ks, vs)
         (o * do).sum().backward()
-        dt = time.perf_counter() - t0
-        best = dt if best is None else min(best, dt)
-    return best, threads
+        times.append(time.perf_counter() - t0)
+    return times, threads
+
+
+def cpu_sample_time(heads=1, reps=1):
+    """Best of `reps` timed samples (see cpu_samples); returns (seconds, threads)."""
+    times, threads = cpu_samples(heads, reps)
+    return min(times), threads
 
 
 def run_reference(args, world, rank):
@@ -375,13 +381,11 @@ def run_ours(args, world, rank, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        # one head of the workload per sample, repeated for ~10 s of CPU work
-        # (median sample; the first, untimed, warms the thread pool)
+        # one head of the workload per sample, repeated until the timed CPU work
+        # adds up to 10 s (median sample; a first, untimed call warms the pool)
         heads = 1
-        _, threads = cpu_sample_time(heads, 1)
-        samples, t_end = [], time.perf_counter() + 10.0
-        while time.perf_counter() < t_end and len(samples) < 1000:
-            samples.append(cpu_sample_time(heads, 1)[0])
+        cpu_sample_time(heads, 1)
+        samples, threads = cpu_samples(heads, 1, seconds=10.0)
         dt = statistics.median(samples)
         cpu = {"value": round(algorithmic_bytes(B, heads, T, D) / dt / 1e9, 3), "unit": "GB/s",
                "cores": threads, "kind": "port",
