@@ -30,7 +30,9 @@
  *     legacy default stream) and never synchronize the host.
  *   - Return value: SQB_OK, or an SQB_ERR_* code for a rejected argument or a
  *     failed launch.  Device-side failures (a bounded wait that gave up) are
- *     recorded in the workspace and read back by sqb_read_status.
+ *     recorded in the workspace, read back (synchronizing) by sqb_read_status,
+ *     and also posted, without any synchronization, to a host-mapped mailbox
+ *     that sqb_attach_status registers with the workspace.
  *   - The workspace belongs to one problem shape (B, T, H, D, block): it
  *     must be zero-filled once before its first use and then passed
  *     unchanged to later calls with that shape (its regions are laid out per
@@ -145,18 +147,46 @@ int sqb_refsem_bwd(const void* q, const void* k, const void* v, const void* dout
  * are those of sqb_bwd without the workspace.  Problems whose
  * sqb_workspace_bytes exceeds 8 MiB return SQB_ERR_WORKSPACE.  The first call on
  * a device looks up the array's address; make it before any stream capture.
- * Each call clears the scratch it uses; all calls on a device share it, so calls
- * that overlap on the GPU race and must not be issued.  Allocates nothing. */
+ * Each call clears the scratch it uses, except a recorded device-side failure,
+ * which stays until sqb_read_status_noalloc reads and clears it; all calls on a
+ * device share the scratch, so calls that overlap on the GPU race and must not
+ * be issued.  Allocates nothing. */
 int sqb_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
                     const void* dout, const float* lse, const void* kbar, const void* vbar,
                     void* dq, void* dk, void* dv, int64_t B, int64_t T, int64_t H, int64_t D,
                     int64_t block, const int64_t* strides, int dtype, float scale, int impl,
                     void* stream);
 
+/* Reads back (after synchronizing `stream`) the device-side status recorded
+ * in the no-allocation scratch of the current device, as sqb_read_status does
+ * for a workspace, and clears it.  sqb_bwd_noalloc keeps a recorded failure
+ * across calls until this call clears it.  No counterpart in the reference. */
+int sqb_read_status_noalloc(void* stream, int64_t* detail);
+
 /* Synchronizes `stream`, returns the device-side status recorded in the
  * workspace (SQB_OK or SQB_ERR_TIMEOUT) and clears it.  `detail`, if not
- * NULL, receives the index of the work tile that reported the failure. */
+ * NULL, receives the work tile index (or wait code) that reported the failure.
+ * A recorded status stays until this call clears it; while it is set, the
+ * kernels' waits on other work tiles give up at once, so the results of later
+ * calls are wrong too: after a failure, zero the workspace again (and attach
+ * the mailbox again).  The reference's kernels have no device-side waits. */
 int sqb_read_status(void* workspace, void* stream, int64_t* detail);
+
+/* Configures a zero-filled workspace before its first use (synchronizes
+ * `stream`; the settings live in the workspace, so zeroing it clears them).
+ * mailbox: NULL, or two uint32 words of page-locked host memory (cudaHostAlloc
+ *   / cudaMallocHost, 8-byte aligned) that the device can write; when a launch
+ *   on this workspace records a failure, its last CTA writes {status, detail}
+ *   there (detail first).  The host polls mailbox[0] without synchronizing
+ *   and, finding it non-zero, knows an earlier call's results are invalid.
+ * wait_budget_us: budget of each kernel wait on another work tile's flag or
+ *   counter, in microseconds (0 = the default of 2 s).  A shorter budget makes
+ *   a lost flag surface sooner; every wait on a CTA's own pipeline keeps its
+ *   own fixed budget.
+ * Has no counterpart in the reference, whose trainer runs the attention as
+ * eager PyTorch ops (model/custom_attention.py:175-230) with nothing to wait on. */
+int sqb_attach_status(void* workspace, uint32_t* mailbox, uint32_t wait_budget_us,
+                      void* stream);
 
 #ifdef __cplusplus
 }

@@ -40,6 +40,8 @@ SIGNATURES = {
                                                             ctypes.c_float, ctypes.c_int, _vp,
                                                             ctypes.c_size_t, _vp]),
     "sqb_read_status": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_c_i64)]),
+    "sqb_read_status_noalloc": (ctypes.c_int, [_vp, ctypes.POINTER(_c_i64)]),
+    "sqb_attach_status": (ctypes.c_int, [_vp, _vp, ctypes.c_uint32, _vp]),
     "sqb_bwd_noalloc": (ctypes.c_int, [_vp] * 11 + [_c_i64] * 5 + [ctypes.POINTER(_c_i64),
                                                                     ctypes.c_int, ctypes.c_float,
                                                                     ctypes.c_int, _vp]),

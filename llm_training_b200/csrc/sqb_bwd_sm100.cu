@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   uint32_t* status = p.ctrl + kStatus;
   const uint32_t token = *reinterpret_cast<volatile uint32_t*>(p.ctrl + kBwdEpoch) + 1u;
+  const uint64_t xbudget = cross_wait_budget(p.ctrl);
   constexpr int kAtoms = D / 64;
   // summary gradients with TMEM lanes = features (needs M = D = 128)
   constexpr bool kTransposedSums = D == 128;
@@ -719,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_wait(&sm.red_done, tc & 1, status, 0x81000000u);
       if (lane == 0) ptx::red_release_add(p.flags + (size_t)t.bh * p.flags_stride + t.s, 1u);
       ptx::counters_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s + 1, NT, token,
-                               status, (uint32_t)n);
+                               status, (uint32_t)n, xbudget);
       if (tc > 0) ptx::mbar_wait(&sm.sgrad_free, (tc - 1) & 1, status, 0x82000000u);
       constexpr bool split = kSplit;
       const int nb = split ? 1 : p.g.R / p.g.b;  // blocks the tile's rows cover
@@ -776,6 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicExch(p.ctrl + kBwdExitCounter, 0u);
       __threadfence();
       atomicExch(p.ctrl + kBwdEpoch, token);
+      post_status(p.ctrl);
     }
   }
 }

@@ -62,7 +62,7 @@ using namespace sqb;
 
 extern "C" {
 
-int sqb_version(void) { return 100; }
+int sqb_version(void) { return 101; }
 
 const char* sqb_strerror(int code) {
   switch (code) {
@@ -156,14 +156,43 @@ int sqb_bwd(const void* q, const void* k, const void* v, const void* o, const vo
 int sqb_read_status(void* workspace, void* stream, int64_t* detail) {
   if (!workspace) return SQB_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  uint32_t words[2] = {0, 0};
+  uint32_t words[3] = {0, 0, 0};
   if (cudaStreamSynchronize(s) != cudaSuccess) return SQB_ERR_CUDA;
   uint8_t* base = (uint8_t*)workspace + kStatus * 4;
   if (cudaMemcpy(words, base, sizeof(words), cudaMemcpyDeviceToHost) != cudaSuccess)
     return SQB_ERR_CUDA;
-  if (words[0] != 0 && cudaMemset(base, 0, sizeof(words)) != cudaSuccess) return SQB_ERR_CUDA;
+  // status, detail and the abort word (normally already cleared by the launch)
+  if ((words[0] | words[2]) != 0 && cudaMemset(base, 0, sizeof(words)) != cudaSuccess)
+    return SQB_ERR_CUDA;
   if (detail) *detail = (int64_t)words[1];
   return (int)words[0];
+}
+
+int sqb_attach_status(void* workspace, uint32_t* mailbox, uint32_t wait_budget_us,
+                      void* stream) {
+  if (!workspace) return SQB_ERR_ARG;
+  uint64_t mb = 0;
+  if (mailbox) {
+    // the device's address of the caller's page-locked pair (equal to the host
+    // address under unified addressing)
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, mailbox) != cudaSuccess) {
+      cudaGetLastError();
+      return SQB_ERR_ARG;
+    }
+    void* dptr = attr.devicePointer;
+    if (attr.type != cudaMemoryTypeHost || !dptr) return SQB_ERR_ARG;  // not page-locked
+    if ((reinterpret_cast<uintptr_t>(dptr) & 7) != 0) return SQB_ERR_ALIGN;
+    mb = (uint64_t)reinterpret_cast<uintptr_t>(dptr);
+  }
+  const uint32_t words[3] = {wait_budget_us, (uint32_t)(mb & 0xFFFFFFFFull),
+                             (uint32_t)(mb >> 32)};
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* dst = (uint8_t*)workspace + kWaitBudgetUs * 4;
+  if (cudaMemcpyAsync(dst, words, sizeof(words), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return SQB_ERR_CUDA;
+  return SQB_OK;
 }
 
 }  // extern "C"

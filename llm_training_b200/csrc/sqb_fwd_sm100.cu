@@ -1,6 +1,7 @@
 // sm_100a forward kernel of sqrt-block attention.
 //
-// Persistent, warp-specialised, one CTA per SM (320 threads):
+// Persistent, warp-specialised, two CTAs per SM (320 threads each, single
+// buffered; the co-resident CTA hides each one's load and MMA latencies):
 //   warp 0      TMA producer + tile scheduler (atomic tile counter)
 //   warp 1      tcgen05.mma issuer (one thread) and TMEM owner
 //   warps 2-5   softmax + epilogue, one query row (TMEM lane) per thread
@@ -27,8 +28,10 @@
 // the summaries it needs has published.
 // A tile only ever waits on tiles with a smaller index, and tiles are only
 // claimed by running CTAs, so every wait ends; each is still bounded in time
-// and records SQB_ERR_TIMEOUT if it gives up.  Flags carry an epoch token so
-// the workspace needs no clearing between calls.
+// (the workspace may set the budget of the waits on other CTAs) and records
+// SQB_ERR_TIMEOUT if it gives up, which the last CTA to leave posts to the
+// caller's mailbox.  Flags carry an epoch token so the workspace needs no
+// clearing between calls.
 
 #include "sqb_sm100.cuh"
 #include "sqb_sm100_common.cuh"
@@ -110,6 +113,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
   const int lane = threadIdx.x & 31;
   uint32_t* status = p.ctrl + kStatus;
   const uint32_t token = *reinterpret_cast<volatile uint32_t*>(p.ctrl + kFwdEpoch) + 1u;
+  const uint64_t xbudget = cross_wait_budget(p.ctrl);
   constexpr int kAtoms = D / 64;
   constexpr uint32_t kTmemCols = fwd_tmem_cols(D, NS);
   const uint32_t box_bytes = (uint32_t)p.g.R * 128u;  // one atom of an R-row box
@@ -221,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
         // every tile holding one of the needed summaries has published
         const int s_need = summary_tile<kSplit>(p.g, t.ns - 1);
         ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, 0, s_need + 1, token,
-                              status, (uint32_t)n);
+                              status, (uint32_t)n, xbudget);
         if (lane == 0) ptx::fence_proxy_async_global();
         for (int c = 0; c < t.nsc; ++c) {
           const SumChunk sc = sum_chunk(t, c);
@@ -596,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
             // the block's earlier sub-tiles have left their sums (their flags)
             if (last && pw == 0)
               ptx::flags_wait_range(p.flags + (size_t)t.bh * p.flags_stride, t.s - t.sub, t.s,
-                                    token, status, (uint32_t)n);
+                                    token, status, (uint32_t)n, xbudget);
 #pragma unroll 1
             for (int kv = 0; kv < 2; ++kv) {
               if ((ptid & 16) == 0 && cc < D / 8) {
@@ -653,6 +657,7 @@ __global__ void __launch_bounds__(kThreads, (ctas_per_sm<NQ, NKV, NS>()))
       atomicExch(p.ctrl + kFwdExitCounter, 0u);
       __threadfence();
       atomicExch(p.ctrl + kFwdEpoch, token);
+      post_status(p.ctrl);
     }
   }
 }

@@ -55,8 +55,12 @@ enum CtrlWord {
   kBwdEpoch = 8,
   kBwdTileCounter = 9,
   kBwdExitCounter = 10,
-  kStatus = 16,        // 0 = ok, else sqb_status
-  kStatusDetail = 17,  // tile index that set kStatus
+  kStatus = 16,        // 0 = ok, else sqb_status (kept until sqb_read_status clears it)
+  kStatusDetail = 17,  // which wait set kStatus (a wait code, or the work tile's index)
+  kStatusAbort = 18,   // a wait on a CTA's own pipeline gave up (cleared at launch end)
+  kWaitBudgetUs = 19,  // budget of waits on other CTAs in microseconds (0 = 2 s)
+  kMailboxLo = 20,     // host-mapped (status, detail) pair a failed launch posts to,
+  kMailboxHi = 21,     //   low and high halves of its device address (0 = none)
   kCtrlWords = 64
 };
 

@@ -17,7 +17,11 @@
 //    cudaGetSymbolAddress (the host-side symbol is only a stand-in, not a
 //    device pointer).  Make that first call before any stream capture.
 //  * Every call clears the part of the array it uses (cudaMemsetAsync, no
-//    allocation) and then runs the regular backward on it.
+//    allocation) and then runs the regular backward on it - all but the two
+//    status words: a device-side failure (a bounded wait that gave up) stays
+//    recorded until sqb_read_status_noalloc reads and clears it, so the next
+//    call does not wipe it.  Until then later calls give up their waits on
+//    other work tiles at once, and their results are wrong too.
 //  * All calls on a device share the array, so calls that overlap on the GPU
 //    (different streams, or host threads without ordering) race on it and
 //    must not be issued; calls ordered on one stream are fine.
@@ -37,15 +41,26 @@ __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
 
+// CUDA errors of the address lookup that mean the library has no code for
+// this GPU (no sm_100a image), reported like sqb_bwd reports such a device.
+int lookup_error(cudaError_t e) {
+  cudaGetLastError();  // the lookup's error is not left behind for the caller
+  return (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction ||
+          e == cudaErrorInvalidDevice)
+             ? SQB_ERR_DEVICE
+             : SQB_ERR_CUDA;
+}
+
 // Device address of the scratch array on the current device (set up once).
 int scratch_address(void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return SQB_ERR_CUDA;
+  if (cudaError_t e = cudaGetDevice(&dev)) return lookup_error(e);
   if (dev < 0 || dev >= kMaxDevices) return SQB_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return SQB_ERR_CUDA;
+    if (cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch)) return lookup_error(e);
+    if (!p) return SQB_ERR_CUDA;
     g_noalloc_ptr[dev] = p;
   }
   *out = g_noalloc_ptr[dev];
@@ -66,7 +81,19 @@ extern "C" int sqb_bwd_noalloc(const void* q, const void* k, const void* v, cons
   void* scratch = nullptr;
   if (int e = scratch_address(&scratch)) return e;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(scratch, 0, need, s) != cudaSuccess) return SQB_ERR_CUDA;
+  // clear everything but the status and its detail (control words kStatus and
+  // kStatusDetail), which stay until sqb_read_status_noalloc clears them
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  const size_t keep_lo = (size_t)sqb::kStatus * 4, keep_hi = (size_t)(sqb::kStatusDetail + 1) * 4;
+  if (cudaMemsetAsync(base, 0, keep_lo, s) != cudaSuccess ||
+      cudaMemsetAsync(base + keep_hi, 0, need - keep_hi, s) != cudaSuccess)
+    return SQB_ERR_CUDA;
   return sqb_bwd(q, k, v, o, dout, lse, kbar, vbar, dq, dk, dv, B, T, H, D, block, strides, dtype,
                  scale, impl, scratch, need, stream);
+}
+
+extern "C" int sqb_read_status_noalloc(void* stream, int64_t* detail) {
+  void* scratch = nullptr;
+  if (int e = scratch_address(&scratch)) return e;
+  return sqb_read_status(scratch, stream, detail);
 }

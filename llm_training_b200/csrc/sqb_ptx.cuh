@@ -26,16 +26,26 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
-// Wall-clock budget of any single wait inside a kernel before it gives up and
-// records SQB_ERR_TIMEOUT (no wait in these kernels can legitimately take
-// more than a few milliseconds).
+// Status words, relative to the status pointer the waits take:
+//   [0] first failure (0 = ok, else an sqb_status), [1] detail of that failure,
+//   [2] abort: set only when a wait on this CTA's own pipeline (an mbarrier)
+//       gave up, which leaves the CTA's roles out of step with each other.
+constexpr int kStatusDetailWord = 1;
+constexpr int kStatusAbortWord = 2;
+
+// Budget of a wait on the kernel's own pipeline (an mbarrier) before it gives
+// up.  Such a wait ends in microseconds unless the CTA is broken; it may sit
+// behind one wait on another CTA, so it outlasts that budget.
+constexpr uint64_t kMbarWaitBudgetNs = 5000000000ull;  // 5 s
+// Default budget of a wait on another CTA's flag or counter (a launch may set
+// its own through the workspace).
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s
 
-// Records the first failure in the workspace status word (status, detail).
+// Records the first failure in the status words (status, detail).
 __device__ __forceinline__ void record_status(uint32_t* status_word, uint32_t code,
                                               uint32_t detail) {
   if (atomicCAS(status_word, 0u, code) == 0u) {
-    atomicExch(status_word + 1, detail);
+    atomicExch(status_word + kStatusDetailWord, detail);
   }
 }
 
@@ -84,7 +94,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase of `bar` with the given parity to complete.  Gives up
-// after kWaitBudgetNs, records SQB_ERR_TIMEOUT and returns false.
+// after kMbarWaitBudgetNs: records SQB_ERR_TIMEOUT and sets the abort word, so
+// every later mbarrier wait of the launch gives up at once (the CTA unwinds in
+// one budget instead of one per wait), and returns false.  A failed wait on
+// another CTA does not make these waits give up: the CTA's own pipeline stays
+// in step and runs to its end, with wrong values where the failed wait's data
+// were needed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
                                           uint32_t detail) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -92,11 +107,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    // after any recorded failure every wait gives up at once, so a kernel
-    // that lost one wait unwinds in one budget rather than one per wait
-    if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
-    if (globaltimer() - t0 > kWaitBudgetNs) {
+    if (*reinterpret_cast<volatile uint32_t*>(status + kStatusAbortWord) != 0u) return false;
+    if (globaltimer() - t0 > kMbarWaitBudgetNs) {
       record_status(status, SQB_ERR_TIMEOUT, detail);
+      atomicExch(status + kStatusAbortWord, 1u);
       return false;
     }
   }
@@ -134,30 +148,14 @@ __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Spins (with backoff) until *flag == want.  Bounded like mbar_wait.
-__device__ __forceinline__ bool flag_wait(const uint32_t* flag, uint32_t want, uint32_t* status,
-                                          uint32_t detail) {
-  if (ld_acquire_gpu(flag) == want) return true;
-  const uint64_t t0 = globaltimer();
-  uint32_t ns = 32;
-  while (true) {
-    __nanosleep(ns);
-    if (ns < 1024) ns <<= 1;
-    if (ld_acquire_gpu(flag) == want) return true;
-    if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) return false;
-    if (globaltimer() - t0 > kWaitBudgetNs) {
-      record_status(status, SQB_ERR_TIMEOUT, detail);
-      return false;
-    }
-  }
-}
-
 // Warp-collective: spins until flags[lo..hi) all equal `want` (each lane polls
 // every 32nd flag), then __syncwarp so every lane is ordered after all the
-// acquires.  Bounded like mbar_wait; returns false if it gave up.
+// acquires.  Gives up after `budget_ns` (recording SQB_ERR_TIMEOUT), or at once
+// once any failure has been recorded, so a lost flag costs the launch one
+// budget; returns false if it gave up.
 __device__ __forceinline__ bool flags_wait_range(const uint32_t* flags, int lo, int hi,
                                                  uint32_t want, uint32_t* status,
-                                                 uint32_t detail) {
+                                                 uint32_t detail, uint64_t budget_ns) {
   const int lane = threadIdx.x & 31;
   uint64_t t0 = 0;
   bool timed = false;
@@ -177,7 +175,7 @@ __device__ __forceinline__ bool flags_wait_range(const uint32_t* flags, int lo, 
       }
       if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {
         stop = 1;
-      } else if (globaltimer() - t0 > kWaitBudgetNs) {
+      } else if (globaltimer() - t0 > budget_ns) {
         record_status(status, SQB_ERR_TIMEOUT, detail);
         stop = 1;
       }
@@ -199,7 +197,7 @@ __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
 // as flags_wait_range.
 __device__ __forceinline__ bool counters_wait_range(const uint32_t* ctr, int lo, int hi,
                                                     uint32_t want, uint32_t* status,
-                                                    uint32_t detail) {
+                                                    uint32_t detail, uint64_t budget_ns) {
   const int lane = threadIdx.x & 31;
   uint64_t t0 = 0;
   bool timed = false;
@@ -219,7 +217,7 @@ __device__ __forceinline__ bool counters_wait_range(const uint32_t* ctr, int lo,
       }
       if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {
         stop = 1;
-      } else if (globaltimer() - t0 > kWaitBudgetNs) {
+      } else if (globaltimer() - t0 > budget_ns) {
         record_status(status, SQB_ERR_TIMEOUT, detail);
         stop = 1;
       }
@@ -272,15 +270,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uin
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
-}
-
-// Pull a 4-D / 3-D tensor-map box into L2 only (no shared-memory destination).
-__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* m, int c0, int c1, int c2,
-                                                   int c3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
-                   reinterpret_cast<uint64_t>(m)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-               : "memory");
 }
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, const void* src, int c0, int c1,

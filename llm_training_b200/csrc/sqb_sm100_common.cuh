@@ -42,6 +42,33 @@ struct Tile {
 
 __host__ __device__ inline int round16(int x) { return (x + 15) & ~15; }
 
+// Budget of this launch's waits on other CTAs: the workspace's setting, else 2 s.
+__device__ inline uint64_t cross_wait_budget(const uint32_t* ctrl) {
+  const uint32_t us = *reinterpret_cast<const volatile uint32_t*>(ctrl + kWaitBudgetUs);
+  return us ? (uint64_t)us * 1000ull : ptx::kWaitBudgetNs;
+}
+
+// Run by the last CTA to leave a launch.  A failure recorded by the launch is
+// posted to the caller's host-mapped mailbox (detail first, then the status
+// word the host polls), so the host learns of it without synchronizing; the
+// abort word is cleared, since the next launch's pipelines start in step.
+// The status word itself stays until sqb_read_status clears it.
+__device__ inline void post_status(uint32_t* ctrl) {
+  volatile uint32_t* c = ctrl;
+  const uint32_t st = c[kStatus];
+  if (st != 0u) {
+    const uint64_t mb = ((uint64_t)c[kMailboxHi] << 32) | (uint64_t)c[kMailboxLo];
+    if (mb != 0ull) {
+      volatile uint32_t* m = reinterpret_cast<volatile uint32_t*>(mb);
+      m[1] = c[kStatusDetail];
+      __threadfence_system();
+      m[0] = st;
+      __threadfence_system();
+    }
+  }
+  c[kStatusAbort] = 0u;
+}
+
 // kSplit: the geometry has b > 128 (kernels are compiled for one case or the
 // other, so the b <= 128 path carries no sub-tile logic).
 template <bool kSplit>

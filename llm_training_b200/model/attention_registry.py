@@ -1,22 +1,27 @@
 """Attention plugin registry: the drop-in boundary of the reference trainer.
 
-Same public API and semantics as the reference's model/attention_registry.py:
-``BaseAttention`` (:39-56), ``register_attention`` (:67-90; names normalised
-case-insensitively with '-' == '_', :63-64; a name already bound to another
-class raises ValueError, :80-86; non-BaseAttention classes raise TypeError,
-:74-78), lazy package discovery (:93-107), the ``module:Class`` escape hatch
-(:110-120), ``available_attentions`` (:123-126), ``get_attention`` (:129-141,
-KeyError listing the registered names) and ``build_attention`` (:144-151,
-``config.attention`` defaulting to "vanilla").
+Public API (what a trainer written against the reference's
+model/attention_registry.py calls, :39-151): ``BaseAttention``,
+``register_attention(*names)``, ``get_attention(name)``,
+``build_attention(config)`` and ``available_attentions()``, with the same
+contract - names compare case-insensitively with '-' and '_' equivalent, a
+name already taken by another class raises ValueError, a class that is not a
+BaseAttention raises TypeError, an unknown name raises KeyError listing the
+known ones, a 'package.module:ClassName' string loads a class directly, and
+``build_attention`` reads ``config.attention`` (default "vanilla").
 
-One deliberate difference: discovery imports each module inside a try block
-and records (rather than propagates) an import failure.  In the reference a
-single broken module (model/flash_attention.py:5) makes the first lookup raise
-for every attention.  ``discovery_errors()`` reports what was skipped.
+Design.  One ``AttentionRegistry`` object holds the name table and the
+plugin discovery state.  Discovery runs once, on the first lookup: every
+module of this package (and any module named in ``extra_plugins``) is
+imported so its ``@register_attention`` decorators run.  A plugin module that
+fails to import is recorded in the ``DiscoveryReport`` (``discovery_errors()``)
+instead of aborting the lookup - unlike the reference, where one broken module
+(model/flash_attention.py:5) makes the first lookup of every name raise.
 """
 
 from __future__ import annotations
 
+import dataclasses
 import importlib
 import pkgutil
 
@@ -39,93 +44,126 @@ class BaseAttention(nn.Module):
         raise NotImplementedError
 
 
-_REGISTRY: dict[str, type] = {}
-_discovered = False
-_discovery_errors: dict[str, str] = {}
+@dataclasses.dataclass
+class DiscoveryReport:
+    """Outcome of the plugin scan: modules imported and modules that failed."""
+
+    imported: list = dataclasses.field(default_factory=list)
+    failed: dict = dataclasses.field(default_factory=dict)  # module -> "Error: message"
 
 
-def _normalize(name):
-    return name.strip().lower().replace("-", "_")
+class AttentionRegistry:
+    """Canonical name -> attention class, filled by plugin modules on import."""
+
+    def __init__(self, package: str, extra_plugins=()):
+        self.package = package
+        self.extra_plugins = list(extra_plugins)
+        self._classes: dict[str, type] = {}
+        self._report: DiscoveryReport | None = None
+
+    @staticmethod
+    def canonical(name: str) -> str:
+        """'Sqrt-Block ' and 'sqrt_block' name the same attention."""
+        return "_".join(name.strip().lower().split("-"))
+
+    # -- registration ------------------------------------------------------------
+    def add(self, cls, names) -> None:
+        if not isinstance(cls, type) or not issubclass(cls, BaseAttention):
+            raise TypeError(f"cannot register {cls!r}: attention plugins must derive from "
+                            "BaseAttention (profilers find the attention layers through it)")
+        keys = [self.canonical(n) for n in names]
+        for key, name in zip(keys, names):
+            holder = self._classes.get(key)
+            if holder not in (None, cls):
+                raise ValueError(f"attention name {name!r} is already registered to "
+                                 f"{holder.__module__}.{holder.__qualname__}")
+        self._classes.update(dict.fromkeys(keys, cls))
+
+    def remove(self, name: str) -> None:
+        self._classes.pop(self.canonical(name), None)
+
+    # -- discovery ---------------------------------------------------------------
+    def _plugin_modules(self):
+        pkg = importlib.import_module(self.package)
+        own = f"{self.package}.attention_registry"
+        found = [f"{self.package}.{m.name}" for m in pkgutil.iter_modules(pkg.__path__)
+                 if not m.name.startswith("_")]
+        return [m for m in found if m != own] + self.extra_plugins
+
+    def scan(self, force: bool = False) -> DiscoveryReport:
+        """Import the plugin modules (once, or again with force=True)."""
+        if self._report is not None and not force:
+            return self._report
+        report = DiscoveryReport()
+        self._report = report  # plugins imported below look names up through us
+        for module in self._plugin_modules():
+            try:
+                importlib.import_module(module)
+            except Exception as exc:  # recorded: one broken plugin hides no other
+                report.failed[module] = f"{type(exc).__name__}: {exc}"
+            else:
+                report.imported.append(module)
+        return report
+
+    # -- lookup ------------------------------------------------------------------
+    def names(self) -> list:
+        self.scan()
+        return sorted(self._classes)
+
+    def resolve(self, name: str) -> type:
+        if ":" in name:
+            return _class_from_spec(name)
+        self.scan()
+        cls = self._classes.get(self.canonical(name))
+        if cls is None:
+            raise KeyError(f"no attention is registered as {name!r} (known: "
+                           f"{', '.join(self.names()) or 'none'}); a module in "
+                           f"{self.package} that registers a BaseAttention subclass with "
+                           "@register_attention(...) adds one")
+        return cls
+
+
+def _class_from_spec(spec: str) -> type:
+    """'package.module:ClassName' -> the class, which must be a BaseAttention."""
+    module_name, class_name = spec.split(":", 1)
+    cls = getattr(importlib.import_module(module_name), class_name, None)
+    if cls is None:
+        raise ValueError(f"{module_name} defines no {class_name!r} (from attention spec "
+                         f"{spec!r})")
+    if not isinstance(cls, type) or not issubclass(cls, BaseAttention):
+        raise TypeError(f"attention spec {spec!r} does not name a BaseAttention subclass")
+    return cls
+
+
+REGISTRY = AttentionRegistry(__name__.rsplit(".", 1)[0])
 
 
 def register_attention(*names):
-    """Class decorator registering an attention under one or more names."""
+    """Class decorator: register the class under every name given."""
 
     def decorator(cls):
-        if not (isinstance(cls, type) and issubclass(cls, BaseAttention)):
-            raise TypeError(
-                f"{getattr(cls, '__name__', cls)} must subclass BaseAttention to be registered "
-                "(profilers find attention layers by that base class)")
-        for name in names:
-            key = _normalize(name)
-            existing = _REGISTRY.get(key)
-            if existing is not None and existing is not cls:
-                raise ValueError(
-                    f"attention name {name!r} is already registered to "
-                    f"{existing.__module__}.{existing.__name__}")
-            _REGISTRY[key] = cls
+        REGISTRY.add(cls, names)
         return cls
 
     return decorator
 
 
-def _discover():
-    """Import every module of this package once so that decorators run."""
-    global _discovered
-    if _discovered:
-        return
-    _discovered = True  # set first: the imports below re-enter this module
-    package = importlib.import_module(__package__)
-    for info in pkgutil.walk_packages(package.__path__, prefix=f"{__package__}."):
-        if info.name == __name__ or info.name.rsplit(".", 1)[-1].startswith("_"):
-            continue
-        try:
-            importlib.import_module(info.name)
-        except Exception as exc:  # a broken plugin must not hide the others
-            _discovery_errors[info.name] = f"{type(exc).__name__}: {exc}"
-
-
-def discovery_errors():
-    """Modules skipped by discovery, with the error each raised."""
-    _discover()
-    return dict(_discovery_errors)
-
-
-def _load_from_path(spec):
-    """Resolve a 'module.path:ClassName' spec into a class."""
-    module_path, _, class_name = spec.partition(":")
-    module = importlib.import_module(module_path)
-    try:
-        cls = getattr(module, class_name)
-    except AttributeError:
-        raise ValueError(f"module {module_path!r} has no attribute {class_name!r}") from None
-    if not (isinstance(cls, type) and issubclass(cls, BaseAttention)):
-        raise TypeError(f"{spec} must be a BaseAttention subclass")
-    return cls
-
-
 def available_attentions():
-    """Sorted list of registered names."""
-    _discover()
-    return sorted(_REGISTRY)
+    """Sorted canonical names of every registered attention."""
+    return REGISTRY.names()
 
 
 def get_attention(name):
-    """Look up a registered attention class by name (or 'module:Class' path)."""
-    if ":" in name:
-        return _load_from_path(name)
-    _discover()
-    try:
-        return _REGISTRY[_normalize(name)]
-    except KeyError:
-        raise KeyError(
-            f"unknown attention {name!r}; available: {', '.join(available_attentions())}. "
-            "Add a new one by dropping a module in this package with a "
-            "@register_attention(...) BaseAttention subclass.") from None
+    """The attention class registered as ``name``, or loaded from 'module:Class'."""
+    return REGISTRY.resolve(name)
 
 
 def build_attention(config, name=None):
-    """Instantiate the attention selected by ``config.attention`` (or ``name``)."""
-    if name is None:
-        name = getattr(config, "attention", "vanilla")
-    return get_attention(name)(config)
+    """An instance of the attention ``config.attention`` (or ``name``) names."""
+    return get_attention(name if name is not None else getattr(config, "attention", "vanilla"))(
+        config)
+
+
+def discovery_errors():
+    """Plugin modules that failed to import during discovery, with their error."""
+    return dict(REGISTRY.scan().failed)

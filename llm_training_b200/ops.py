@@ -11,12 +11,14 @@ from __future__ import annotations
 
 import math
 import threading
+from typing import Optional
 
 import torch
 
 from . import _lib
 
 __all__ = ["sqrt_block_attention", "sqrt_block_forward", "sqrt_block_backward", "read_status",
+           "check_status", "set_wait_budget_us",
            "block_geometry", "reference_attention", "reference_forward", "reference_backward",
            "cross_entropy", "layer_norm", "layer_norm_supported"]
 
@@ -24,6 +26,11 @@ _DTYPES = {torch.float32: _lib.SQB_F32, torch.bfloat16: _lib.SQB_BF16}
 
 _ws_lock = threading.Lock()
 _workspaces: dict[tuple, torch.Tensor] = {}
+# per workspace: two page-locked int32 words (status, detail) the kernels post a
+# device-side failure to; polled without synchronizing
+_mailboxes: dict[tuple, torch.Tensor] = {}
+_mailbox_words: dict[tuple, "object"] = {}  # numpy views of the same words (cheap reads)
+_wait_budget_us = 0  # 0 = the library default (2 s)
 
 
 def block_geometry(T: int, block: int | None = None):
@@ -31,13 +38,22 @@ def block_geometry(T: int, block: int | None = None):
     return _lib.geometry(T, block)
 
 
+def _attach(key) -> None:
+    ws, mb = _workspaces[key], _mailboxes[key]
+    stream = torch.cuda.current_stream(ws.device).cuda_stream
+    _lib.check("sqb_attach_status", _lib.lib().sqb_attach_status(
+        ws.data_ptr(), mb.data_ptr(), _wait_budget_us, stream))
+
+
 def _workspace(device: torch.device, shape: tuple) -> torch.Tensor:
     """Zero-initialised scratch for one (B, T, H, D, b) problem on one device.
 
     The kernels keep it clean between calls (flags are epoch-stamped and the
     summary-gradient accumulators end every call at zero), so it is zeroed
-    only when allocated.  The region layout depends on the problem shape,
-    hence one workspace per shape.  Calls on one device must share one stream.
+    only when allocated, and again after a device-side failure.  The region
+    layout depends on the problem shape, hence one workspace per shape.  Calls
+    on one device must share one stream.  Each workspace has a page-locked
+    mailbox the kernels post a device-side failure to (``check_status``).
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
     key = (idx,) + tuple(int(x) for x in shape)
@@ -47,7 +63,57 @@ def _workspace(device: torch.device, shape: tuple) -> torch.Tensor:
             nbytes = _lib.workspace_bytes(*shape)
             ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
             _workspaces[key] = ws
+            _mailboxes[key] = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+            _mailbox_words[key] = _mailboxes[key].numpy()
+            _attach(key)
         return ws
+
+
+def _reset(key) -> None:
+    """Zero a workspace (and its mailbox) after a device-side failure."""
+    _workspaces[key].zero_()
+    _mailboxes[key].zero_()
+    _attach(key)
+
+
+def check_status(device=None) -> None:
+    """Raise ``SqrtBlockError`` (code SQB_ERR_TIMEOUT) if a kernel launched on
+    ``device`` (default: every device) posted a device-side failure - a
+    bounded wait that gave up, which leaves that call's outputs invalid.
+
+    Never synchronizes: it reads the page-locked mailboxes the kernels write
+    when they finish, so it reports failures of calls that have completed on
+    the GPU by the time it runs (a call still in flight is reported by a later
+    check).  Every op of this module runs it on entry, and the GPT trainer
+    once per step.  The failed workspace is zeroed again before raising, so
+    calls after the error compute correct results.
+    """
+    idx = None
+    if device is not None:
+        idx = device if isinstance(device, int) else (
+            device.index if device.index is not None else torch.cuda.current_device())
+    for key, mb in list(_mailbox_words.items()):
+        if mb[0] == 0 or (idx is not None and key[0] != idx):
+            continue
+        code, detail = int(mb[0]), int(mb[1]) & 0xFFFFFFFF
+        with _ws_lock:
+            _reset(key)
+        raise _lib.SqrtBlockError(
+            "sqrt-block attention", code,
+            f"{_lib.lib().sqb_strerror(code).decode()} in an earlier call on device {key[0]} "
+            f"(problem (B, T, H, D, b) = {key[1:]}, detail {detail:#x}); that call's outputs "
+            "are invalid, and its workspace has been reset")
+
+
+def set_wait_budget_us(microseconds: int) -> None:
+    """Budget of the kernels' waits on other work tiles (0 = the library
+    default of 2 s), for every workspace of this process."""
+    global _wait_budget_us
+    _wait_budget_us = int(microseconds)
+    with _ws_lock:
+        for key in list(_workspaces):
+            with torch.cuda.device(key[0]):
+                _attach(key)
 
 
 def _strides(t: torch.Tensor):
@@ -91,6 +157,8 @@ def sqrt_block_forward(q, k, v, block=None, scale=None, impl="auto"):
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     dev = q.device
+    if _mailbox_words:
+        check_status(dev)
     o = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
     lse = torch.empty((B, H, T), dtype=torch.float32, device=dev)
     kbar = torch.empty((B, H, Gc, D), dtype=q.dtype, device=dev)
@@ -119,6 +187,8 @@ def sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block=None, scale=Non
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     dev = q.device
+    if _mailbox_words:
+        check_status(dev)
     dq = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
     dk = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
     dv = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
@@ -138,7 +208,9 @@ def sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block=None, scale=Non
 
 def read_status(device=None) -> int:
     """Synchronize and return (then clear) the first device-side status
-    recorded in any workspace of the device (0 = ok)."""
+    recorded in any workspace of the device (0 = ok); a workspace that
+    recorded a failure is zeroed again.  ``check_status`` is the
+    non-synchronizing check."""
     idx = device if isinstance(device, int) else (
         device.index if device is not None and device.index is not None
         else torch.cuda.current_device())
@@ -150,30 +222,80 @@ def read_status(device=None) -> int:
             continue
         detail = _lib.ctypes.c_int64()
         rc = _lib.lib().sqb_read_status(ws.data_ptr(), stream, _lib.ctypes.byref(detail))
-        if rc != _lib.SQB_OK and status == _lib.SQB_OK:
-            status = rc
+        if rc != _lib.SQB_OK:
+            if status == _lib.SQB_OK:
+                status = rc
+            with _ws_lock:
+                _reset(key)
     return status
 
 
-class _SqrtBlockAttention(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, q, k, v, block, scale, impl):
-        o, lse, kbar, vbar = sqrt_block_forward(q, k, v, block, scale, impl)
-        ctx.save_for_backward(q, k, v, o, lse, kbar, vbar)
-        ctx.cfg = (block, scale, impl)
-        return o
+# ---- custom ops: the boundary as torch.library operators ----------------------
+# The op is registered with torch.library (a fake implementation for tracing,
+# autograd through the library's backward), so torch.compile - the reference
+# trainer's default (train.py:28-30, :370) - traces a model using it as one
+# opaque node per call instead of breaking the graph at every layer.
 
-    @staticmethod
-    def backward(ctx, dout):
-        q, k, v, o, lse, kbar, vbar = ctx.saved_tensors
-        block, scale, impl = ctx.cfg
-        dq, dk, dv = sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block, scale, impl)
-        return dq, dk, dv, None, None, None
+
+def _fake_geometry(T, block):
+    # pure-Python twin of the library's sqb_geometry (b = round_up(ceil(sqrt(T)), 16))
+    T = int(T)
+    b = int(block) if block else (math.isqrt(T - 1) + 1 + 15) // 16 * 16
+    return b, -(-T // b), T // b
+
+
+@torch.library.custom_op("sqrtblock::attention_fwd", mutates_args=())
+def _attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block: Optional[int],
+                   scale: Optional[float], impl: str
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    return sqrt_block_forward(q, k, v, block, scale, impl)
+
+
+@_attention_fwd.register_fake
+def _(q, k, v, block, scale, impl):
+    B, T, H, D = q.shape
+    _, _, Gc = _fake_geometry(T, block)
+    return (q.new_empty((B, T, H, D)), q.new_empty((B, H, T), dtype=torch.float32),
+            q.new_empty((B, H, Gc, D)), q.new_empty((B, H, Gc, D)))
+
+
+@torch.library.custom_op("sqrtblock::attention_bwd", mutates_args=())
+def _attention_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+                   lse: torch.Tensor, kbar: torch.Tensor, vbar: torch.Tensor,
+                   dout: torch.Tensor, block: Optional[int], scale: Optional[float], impl: str
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block, scale, impl)
+
+
+@_attention_bwd.register_fake
+def _(q, k, v, o, lse, kbar, vbar, dout, block, scale, impl):
+    return tuple(q.new_empty(q.shape) for _ in range(3))
+
+
+def _attention_setup(ctx, inputs, output):
+    q, k, v, block, scale, impl = inputs
+    o, lse, kbar, vbar = output
+    ctx.save_for_backward(q, k, v, o, lse, kbar, vbar)
+    ctx.cfg = (block, scale, impl)
+    ctx.mark_non_differentiable(lse, kbar, vbar)
+
+
+def _attention_grad(ctx, dout, _dlse, _dkbar, _dvbar):
+    q, k, v, o, lse, kbar, vbar = ctx.saved_tensors
+    dq, dk, dv = _attention_bwd(q, k, v, o, lse, kbar, vbar, dout, *ctx.cfg)
+    return dq, dk, dv, None, None, None
+
+
+_attention_fwd.register_autograd(_attention_grad, setup_context=_attention_setup)
 
 
 def sqrt_block_attention(q, k, v, block=None, scale=None, impl="auto"):
-    """Differentiable sqrt-block attention on (B, T, H, D) CUDA views -> O (B, T, H, D)."""
-    return _SqrtBlockAttention.apply(q, k, v, block, scale, impl)
+    """Differentiable sqrt-block attention on (B, T, H, D) CUDA views -> O (B, T, H, D).
+
+    One ``sqrtblock::attention_fwd`` custom op (its backward is
+    ``sqrtblock::attention_bwd``); LSE and the block summaries it also returns
+    are saved for the backward and are not differentiable."""
+    return _attention_fwd(q, k, v, block, scale, impl)[0]
 
 
 # ---- reference-semantics mode ---------------------------------------------------
@@ -265,24 +387,53 @@ def reference_backward(q, k, v, glob, summary, dout, scale=None):
     return dq, dk, dv
 
 
-class _ReferenceAttention(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, q, k, v, scale):
-        o, glob, summary = reference_forward(q, k, v, scale)
-        ctx.save_for_backward(q, k, v, glob, summary)
-        ctx.scale = scale
-        return o
+@torch.library.custom_op("sqrtblock::reference_fwd", mutates_args=())
+def _reference_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float]
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return reference_forward(q, k, v, scale)
 
-    @staticmethod
-    def backward(ctx, dout):
-        q, k, v, glob, summary = ctx.saved_tensors
-        dq, dk, dv = reference_backward(q, k, v, glob, summary, dout, ctx.scale)
-        return dq, dk, dv, None
+
+@_reference_fwd.register_fake
+def _(q, k, v, scale):
+    B, T, H, D = q.shape
+    L = _refsem_check_T(int(T))
+    return (q.new_empty((B, T, H, D)), q.new_empty((B, H, L, L), dtype=torch.float32),
+            q.new_empty((B, H, L, L), dtype=torch.float32))
+
+
+@torch.library.custom_op("sqrtblock::reference_bwd", mutates_args=())
+def _reference_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, glob: torch.Tensor,
+                   summary: torch.Tensor, dout: torch.Tensor, scale: Optional[float]
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return reference_backward(q, k, v, glob, summary, dout, scale)
+
+
+@_reference_bwd.register_fake
+def _(q, k, v, glob, summary, dout, scale):
+    return tuple(q.new_empty(q.shape) for _ in range(3))
+
+
+def _reference_setup(ctx, inputs, output):
+    q, k, v, scale = inputs
+    o, glob, summary = output
+    ctx.save_for_backward(q, k, v, glob, summary)
+    ctx.scale = scale
+    ctx.mark_non_differentiable(glob, summary)
+
+
+def _reference_grad(ctx, dout, _dglob, _dsummary):
+    q, k, v, glob, summary = ctx.saved_tensors
+    dq, dk, dv = _reference_bwd(q, k, v, glob, summary, dout, ctx.scale)
+    return dq, dk, dv, None
+
+
+_reference_fwd.register_autograd(_reference_grad, setup_context=_reference_setup)
 
 
 def reference_attention(q, k, v, scale=None):
-    """Differentiable reference-semantics attention on (B, T, H, D) CUDA views -> O."""
-    return _ReferenceAttention.apply(q, k, v, scale)
+    """Differentiable reference-semantics attention on (B, T, H, D) CUDA views -> O
+    (the ``sqrtblock::reference_fwd`` custom op)."""
+    return _reference_fwd(q, k, v, scale)[0]
 
 
 # ---- training caller: fused token cross-entropy (include/sqb_train.h) ------------

@@ -19,7 +19,7 @@ import torch
 import torch.nn.functional as F
 
 from .model.gpt import GPT
-from .ops import cross_entropy
+from .ops import check_status, cross_entropy
 
 
 def calculate_loss(logits, targets):
@@ -74,6 +74,11 @@ class Trainer:
         self.autocast = autocast and device.type == "cuda"
 
     def step(self, x, y):
+        """One optimizer step.  First raises if an attention kernel of an earlier
+        step posted a device-side failure (a non-blocking check of the
+        library's page-locked mailboxes: that step's gradients were invalid)."""
+        if self.device.type == "cuda":
+            check_status(self.device)
         self.optimizer.zero_grad(set_to_none=True)
         with torch.autocast(device_type=self.device.type, dtype=torch.bfloat16,
                             enabled=self.autocast):

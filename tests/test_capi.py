@@ -73,3 +73,9 @@ def test_fwd_argument_errors_need_no_device():
 def test_check_raises_with_message():
     with pytest.raises(_lib.SqrtBlockError, match="workspace"):
         _lib.check("sqb_fwd", 5)
+
+
+def test_status_entry_points_reject_a_missing_workspace():
+    lib = _lib.lib()
+    assert lib.sqb_read_status(None, None, None) == 1      # SQB_ERR_ARG
+    assert lib.sqb_attach_status(None, None, 0, None) == 1

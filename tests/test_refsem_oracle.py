@@ -71,3 +71,22 @@ def test_oracle_block0_is_local_attention_and_causal():
 def test_geometry_rejects_non_squares(T):
     with pytest.raises(ValueError, match="perfect square"):
         rso.geometry(T)
+
+
+def test_torch_port_matches_oracle():
+    """The torch restatement timed as the refsem reference arm agrees with the
+    float64 oracle (which is pinned to the reference module's own outputs)."""
+    import torch
+
+    from oracle.refsem_torch_port import reference_core
+
+    g = np.random.default_rng(5)
+    q, k, v, do = (g.standard_normal((2, 3, 256, 32)) for _ in range(4))
+    ro, _, _ = rso.fwd(q, k, v)
+    rq, rk, rv = rso.bwd(q, k, v, do)
+    tq, tk, tv = (torch.from_numpy(x).requires_grad_(True) for x in (q, k, v))
+    out = reference_core(tq, tk, tv)
+    (out * torch.from_numpy(do)).sum().backward()
+    assert np.abs(out.detach().numpy() - ro).max() < 1e-10
+    for a, r in ((tq, rq), (tk, rk), (tv, rv)):
+        assert np.abs(a.grad.numpy() - r).max() < 1e-10

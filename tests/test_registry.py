@@ -43,7 +43,7 @@ def test_register_rejects_non_base_and_duplicates():
         @reg.register_attention("zz_test_attn")
         class B(reg.BaseAttention):
             pass
-    del reg._REGISTRY["zz_test_attn"]
+    reg.REGISTRY.remove("zz_test_attn")
 
 
 def test_module_class_escape_hatch():
@@ -56,20 +56,18 @@ def test_module_class_escape_hatch():
 
 
 def test_discovery_isolates_broken_modules(monkeypatch):
-    import pkgutil
-
-    real = pkgutil.walk_packages
-
-    def fake(path, prefix=""):
-        yield from real(path, prefix)
-        yield pkgutil.ModuleInfo(None, prefix + "zz_missing_module", False)
-
-    monkeypatch.setattr(reg, "_discovered", False)
-    monkeypatch.setattr(reg, "_discovery_errors", {})
-    monkeypatch.setattr(pkgutil, "walk_packages", fake)
-    assert "sqrt_block" in reg.available_attentions()  # still found
-    errs = reg.discovery_errors()
-    assert any("zz_missing_module" in k for k in errs)
+    monkeypatch.setattr(reg.REGISTRY, "extra_plugins", ["zz_missing_module"])
+    report = reg.REGISTRY.scan(force=True)
+    try:
+        assert "zz_missing_module" in report.failed
+        assert "ModuleNotFoundError" in report.failed["zz_missing_module"]
+        assert any(m.endswith(".sqrt_block_attention") for m in report.imported)
+        assert "sqrt_block" in reg.available_attentions()  # still found
+        assert "zz_missing_module" in reg.discovery_errors()
+    finally:
+        monkeypatch.undo()
+        reg.REGISTRY.scan(force=True)
+    assert reg.discovery_errors() == {}
 
 
 def test_build_attention_uses_config_name():

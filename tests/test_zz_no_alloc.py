@@ -10,6 +10,7 @@ call checks that each call clears what it needs).  This file is collected
 last so that a run stopping at its first failure has run every other test.
 """
 
+import ctypes
 import math
 
 import pytest
@@ -53,6 +54,8 @@ def close(got, ref, dtype):
     (torch.bfloat16, (2, 1024, 4, 64), 32),
     (torch.bfloat16, (1, 4096, 2, 128), None),
     (torch.bfloat16, (1, 1000, 2, 128), 128),
+    # b > 128: the cross sub-tile dK / dV and reader-count regions of the scratch
+    (torch.bfloat16, (1, 4096, 2, 128), 192),
     (torch.float32, (2, 256, 4, 32), 16),
 ])
 def test_noalloc_matches_workspace_backward(dtype, shape, block):
@@ -65,6 +68,11 @@ def test_noalloc_matches_workspace_backward(dtype, shape, block):
         torch.cuda.synchronize()
         for name, a, r in zip(("dq", "dk", "dv"), got, ref):
             assert close(a, r, dtype), name
+    # no device-side failure was recorded in the library's scratch
+    detail = ctypes.c_int64(-1)
+    assert _lib.lib().sqb_read_status_noalloc(torch.cuda.current_stream().cuda_stream,
+                                              ctypes.byref(detail)) == 0
+    assert detail.value == 0
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
