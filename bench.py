@@ -631,6 +631,7 @@ def train_record(args, workload, world, rank, local, steps, warmup):
     from llm_training_b200.train import Trainer, synthetic_batch
 
     kind, batch, seq = TRAIN_WORKLOADS[workload]
+    batch = args.train_batch or batch
     cfg = gpt2_small(block_size=seq) if kind == "small" else gpt2_medium(block_size=seq,
                                                                         sqrt_block_b=96)
     dev = torch.device("cuda", local)
@@ -718,9 +719,39 @@ def train_record(args, workload, world, rank, local, steps, warmup):
                   "d2h_bytes_per_step": 4, "steps": e_steps,
                   "timing": "host clock, loss.item() every step, max over ranks"}
     rec["last_loss"] = round(float(lv), 4)
+    if getattr(args, "metrics_out", None):
+        rec["metrics_json"] = write_report(args, tr, cfg, host, batch, seq, world, rank, dev)
     del tr
     torch.cuda.empty_cache()
     return rec
+
+
+def write_report(args, tr, cfg, host, batch, seq, world, rank, dev):
+    """A run in the reference trainer's metrics.json schema (written by rank 0):
+    the host batch copied in ("data"), forward, backward and optimizer phases,
+    attention layers hooked, the first 5 steps excluded from the means."""
+    from llm_training_b200.metrics import MetricsReport
+    from llm_training_b200.model.attention_registry import BaseAttention
+
+    steps = max(args.report_steps, 6)
+    info = tr.run_info(cfg, batch, seq, max_steps=steps, lr=6e-4, seed=1337)
+    info["data_parallel_ranks"] = world
+    rep = MetricsReport(args.metrics_out if rank == 0 else None, info,
+                        tokens_per_step=batch * seq * world, warmup_steps_skipped=5,
+                        log_interval=1, device_type="cuda")
+    rep.attach_attention(tr.raw_model, BaseAttention)
+    for step in range(steps):
+        rep.begin_step(step)
+        with rep.phase("data"):
+            tok = host[step % 2].to(dev, non_blocking=True)
+        loss, norm = tr.step(tok[:, :-1], tok[:, 1:], report=rep)
+        rep.end_step(step, float(loss), 6e-4, float(norm))
+    doc = rep.write("finished")
+    return {"path": args.metrics_out, "measured_steps": doc["aggregates"]["measured_steps"],
+            "avg_tokens_per_sec": doc["aggregates"]["avg_tokens_per_sec"],
+            "attention_fraction_of_step_time":
+                doc["aggregates"].get("attention", {}).get("fraction_of_step_time"),
+            "note": "per-step synchronize and hooks: slower than the timed tokens_per_s"}
 
 
 def run_train(args, world, rank, local):
@@ -746,6 +777,12 @@ def main():
     ap.add_argument("--train-steps", type=int, default=30)
     ap.add_argument("--train-warmup", type=int, default=5)
     ap.add_argument("--h64-steps", type=int, default=30)
+    ap.add_argument("--metrics-out", default=None,
+                    help="gpt2-* workloads: also write a metrics.json report (the reference "
+                         "trainer's schema) of --report-steps profiled steps to this path")
+    ap.add_argument("--report-steps", type=int, default=20)
+    ap.add_argument("--train-batch", type=int, default=0,
+                    help="sequences per GPU of the training workloads (0 = the config's)")
     ap.add_argument("--warmup-seconds", type=float, default=0.5,
                     help="keep warming up at least this long (clock sampler needs samples)")
     ap.add_argument("--workload", choices=sorted(ATTN) + sorted(TRAIN_WORKLOADS) + sorted(REFSEM),

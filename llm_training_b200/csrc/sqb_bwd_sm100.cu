@@ -1,11 +1,11 @@
 // sm_100a backward kernel of sqrt-block attention.
 //
-// Persistent, warp-specialised, one CTA per SM (352 threads):
+// Persistent, warp-specialised, one CTA per SM (32 * (3 + 4 * kParts) threads):
 //   warp 0      TMA producer + tile scheduler
 //   warp 1      tcgen05.mma issuer and TMEM owner
-//   warps 2-9   softmax-gradient / epilogue: two warps per TMEM lane quarter,
-//               one TMEM lane (row) per thread, each warp half of the columns
-//   warp 10     publisher of the summary-gradient counters
+//   warps 2..   softmax-gradient / epilogue: kParts warps per TMEM lane quarter,
+//               one TMEM lane (row) per thread, each warp 1/kParts of the columns
+//   last warp   publisher of the summary-gradient counters
 //
 // A work tile is the same R-row tile as in the forward.  Its chunks are the
 // summary chunks first, then the tile's own (in-block) keys.  Per chunk, with
@@ -35,6 +35,11 @@
 
 #include "sqb_sm100.cuh"
 #include "sqb_sm100_common.cuh"
+
+// Gradient warps per TMEM lane quarter (2 or 4).
+#ifndef SQB_BWD_PARTS
+#define SQB_BWD_PARTS 2
+#endif
 
 namespace sqb {
 namespace sm100 {
@@ -77,7 +82,7 @@ struct BwdSmem {
   // loaded here (the tile's O still occupies the V buffer until delta is done)
   alignas(1024) uint8_t ds[2 * kAtomBytes];
   float sgrad[2][4][D];  // summary gradient / b of the tile's blocks (dK, dV)
-  float dpart[2][128];   // delta = rowsum(dO * O): the two column halves' sums
+  float dpart[4][128];   // delta = rowsum(dO * O): the column parts' sums
   uint64_t ld_full, ld_empty, k_full, k_empty, v_full, v_empty, s_full, ps_full, g_full, g_free;
   uint64_t delta_done, stage_free;
   uint64_t red_done, pub_read, sums_ready, sgrad_free;
@@ -87,7 +92,11 @@ struct BwdSmem {
   uint32_t tmem_base;
 };
 
-constexpr int kThreads = 352;
+// kParts gradient warps per TMEM lane quarter; producer, MMA and publisher warps
+template <int kParts>
+constexpr int bwd_threads() {
+  return 32 * (3 + 4 * kParts);
+}
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -99,8 +108,8 @@ constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256, kColSLast = 384;
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-template <int D, bool kSplit>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, bool kSplit, int kParts>
+__global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                const __grid_constant__ CUtensorMap tm_do,
@@ -117,6 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t token = *reinterpret_cast<volatile uint32_t*>(p.ctrl + kBwdEpoch) + 1u;
   const uint64_t xbudget = cross_wait_budget(p.ctrl);
   constexpr int kAtoms = D / 64;
+  constexpr int kGradWarps = 4 * kParts;
   // summary gradients with TMEM lanes = features (needs M = D = 128)
   constexpr bool kTransposedSums = D == 128;
   const uint32_t box_bytes = (uint32_t)p.g.R * 128u;
@@ -126,19 +136,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(&sm.ld_full, 1);
     ptx::mbar_init(&sm.ld_empty, 1);
     ptx::mbar_init(&sm.delta_done, 1);
-    ptx::mbar_init(&sm.red_done, 8);  // one arrive per gradient warp
+    ptx::mbar_init(&sm.red_done, kGradWarps);  // one arrive per gradient warp
     ptx::mbar_init(&sm.pub_read, 1);
     ptx::mbar_init(&sm.sums_ready, 1);
-    ptx::mbar_init(&sm.sgrad_free, 8);  // one arrive per gradient warp
+    ptx::mbar_init(&sm.sgrad_free, kGradWarps);  // one arrive per gradient warp
     ptx::mbar_init(&sm.k_full, 1);
     ptx::mbar_init(&sm.k_empty, 1);  // dQ MMA of the chunk complete
     ptx::mbar_init(&sm.v_full, 1);
     ptx::mbar_init(&sm.v_empty, 1);  // dP MMA of the chunk complete
     ptx::mbar_init(&sm.stage_free, 1);
     ptx::mbar_init(&sm.s_full, 1);
-    ptx::mbar_init(&sm.ps_full, 8);
+    ptx::mbar_init(&sm.ps_full, kGradWarps);
     ptx::mbar_init(&sm.g_full, 1);
-    ptx::mbar_init(&sm.g_free, 8);
+    ptx::mbar_init(&sm.g_free, kGradWarps);
     ptx::mbar_init(&sm.mma_done, 1);
     ptx::mbar_init(&sm.dq_full, 1);
     ptx::fence_mbarrier_init();
@@ -353,17 +363,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mma_commit(&sm.mma_done);
       ptx::mbar_drain(&sm.mma_done, 0);
     }
-  } else if (warp < 10) {
+  } else if (warp < 2 + kGradWarps) {
     // ------------------------------------------------------------ gradient warps
-    // Eight warps, two per TMEM lane quarter: half h = (warp - 2) / 4 takes key
-    // columns [64h, 64h + 64) of S/dP and columns [h*D/2, (h+1)*D/2) of dK, dV
-    // and dQ, so every per-row loop is half as long as with one warp per quarter.
-    const int gtid = threadIdx.x - 64;  // 0..255
-    const int half = (warp - 2) >> 2;
+    // kParts warps per TMEM lane quarter: part h = (warp - 2) / 4 takes key
+    // columns [h*128/kParts, (h+1)*128/kParts) of S/dP and columns
+    // [h*D/kParts, (h+1)*D/kParts) of dK, dV and dQ, so every per-row loop is
+    // 1/kParts as long as with one warp per quarter.
+    const int gtid = threadIdx.x - 64;  // 0 .. 32 * kGradWarps - 1
+    const int part = (warp - 2) >> 2;   // column part
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane: query row, then key row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    constexpr int kHalfD = D / 2;
+    constexpr int kPartD = D / kParts;        // dK / dV / dQ columns of a part
+    constexpr int kPieces = 128 / kParts / 16;  // 16-column S / dP pieces of a part
+    constexpr int kGradThreads = 32 * kGradWarps;
     int tc = 0, kc = 0;
     while (true) {
       ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x70000000u);
@@ -375,32 +388,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int blk_t = valid ? tq / p.g.b : 0;
       const int lim = valid ? min(blk_t, p.g.Gc) : 0;
       const float L = valid ? p.lse[(size_t)t.bh * p.g.T + tq] * kLog2e : 0.f;
-      // delta = rowsum(dO * O); O was loaded into the V buffer.  Each half sums
-      // its D/2 columns; the halves meet in shared memory.
-      float dhalf = 0.f;
+      // delta = rowsum(dO * O); O was loaded into the V buffer.  Each part sums
+      // its D/kParts columns; the parts meet in shared memory.
+      float dpart_sum = 0.f;
       if (valid) {
 #pragma unroll 4
-        for (int cc = half * (D / 16); cc < (half + 1) * (D / 16); ++cc) {
+        for (int cc = part * (D / 8 / kParts); cc < (part + 1) * (D / 8 / kParts); ++cc) {
           const uint32_t off = swz_offset(row, cc * 8);
           const uint4 a = *reinterpret_cast<const uint4*>(sm.v + off);
           const uint4 g = *reinterpret_cast<const uint4*>(sm.dout + off);
-          dhalf += bf16lo(a.x) * bf16lo(g.x) + bf16hi(a.x) * bf16hi(g.x) +
+          dpart_sum += bf16lo(a.x) * bf16lo(g.x) + bf16hi(a.x) * bf16hi(g.x) +
                    bf16lo(a.y) * bf16lo(g.y) + bf16hi(a.y) * bf16hi(g.y) +
                    bf16lo(a.z) * bf16lo(g.z) + bf16hi(a.z) * bf16hi(g.z) +
                    bf16lo(a.w) * bf16lo(g.w) + bf16hi(a.w) * bf16hi(g.w);
         }
       }
-      sm.dpart[half][row] = dhalf;
+      sm.dpart[part][row] = dpart_sum;
       // the previous tile's dK staging (P buffer) has been read by its TMA
       // store before this tile's P/dS are written (after the barrier)
       if (gtid == 0 && tc > 0) ptx::tma_store_wait_read_all();
       // This tile's O (V buffer) has been consumed into delta: the first V
       // chunk may be loaded.
-      ptx::named_barrier(1, 256);
+      ptx::named_barrier(1, kGradThreads);
       if (gtid == 0) ptx::mbar_arrive(&sm.delta_done);
-      const float delta = sm.dpart[0][row] + sm.dpart[1][row];
+      float delta = sm.dpart[0][row];
+#pragma unroll
+      for (int i = 1; i < kParts; ++i) delta += sm.dpart[i][row];
 
-      // P and dS of one chunk into smem (this half's 64 key columns; masked -> 0)
+      // P and dS of one chunk into smem (this part's key columns; masked -> 0)
       auto softmax_grad = [&](int N, int vlo, int vhi, uint32_t col_s) {
         const bool any_col = vhi > vlo;
         const int wlo = __reduce_min_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
@@ -409,9 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int lo_max = __reduce_max_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
         const int hi_min = __reduce_min_sync(0xffffffffu, any_col ? vhi : 0);
         const float delta_s = delta * p.scale;
-        // this half's four 16-column pieces; a piece is live (warp-uniform)
-        // when it holds a column some row of this warp sees
-        auto col0 = [&](int pi) { return (half * 4 + pi) * 16; };
+        // this part's 16-column pieces; a piece is live (warp-uniform) when it
+        // holds a column some row of this warp sees
+        auto col0 = [&](int pi) { return (part * kPieces + pi) * 16; };
         auto live = [&](int pi) {
           const int c0 = col0(pi);
           return c0 < N && c0 < whi && c0 + 16 > wlo;
@@ -458,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_wait(&sm.s_full, kc & 1, status, 0x71000000u);
         ptx::tc_fence_after();
 #pragma unroll 1
-        for (int pi = 0; pi < 4; ++pi) {
+        for (int pi = 0; pi < kPieces; ++pi) {
           uint32_t sv[16], dp[16];
           load(pi, sv, dp);
           ptx::tmem_wait_ld();
@@ -475,14 +490,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
 
       // Adds this lane's row of a chunk's dKc / dVc (TMEM, S and dP columns,
-      // this warp's column half) to fp32 rows of the workspace with vector
+      // this warp's column part) to fp32 rows of the workspace with vector
       // atomics, then frees the columns for the next chunk's S/dP.
       // store: plain stores instead of atomic additions (a destination with a
       // single writer)
       auto drain = [&](float* dkrow, float* dvrow, bool ok, bool store) {
 #pragma unroll 1
-        for (int pc = 0; pc < kHalfD / 16; ++pc) {
-          const int col0 = half * kHalfD + pc * 16;
+        for (int pc = 0; pc < kPartD / 16; ++pc) {
+          const int col0 = part * kPartD + pc * 16;
           uint32_t gv[16], gk[16];
           ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
           ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
@@ -523,8 +538,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* dvb = p.dvbar + (size_t)t.bh * p.g.Gc * D + row;
         float* dkb = p.dkbar + (size_t)t.bh * p.g.Gc * D + row;
 #pragma unroll 1
-        for (int pc = 0; pc < 4; ++pc) {
-          const int col0 = half * 64 + pc * 16;
+        for (int pc = 0; pc < kPieces; ++pc) {
+          const int col0 = (part * kPieces + pc) * 16;
           if (col0 + 16 <= clo || col0 >= chi) continue;  // warp-uniform
           uint32_t gv[16], gk[16];
           ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
@@ -603,8 +618,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* xrow = (kv ? p.dvx : p.dkx) + xr * D;
           uint8_t* dst = kv ? sm.ds : sm.p;
 #pragma unroll 1
-          for (int pc = 0; pc < kHalfD / 16; ++pc) {
-            const int col0 = half * kHalfD + pc * 16;
+          for (int pc = 0; pc < kPartD / 16; ++pc) {
+            const int col0 = part * kPartD + pc * 16;
             uint32_t g[16];
             ptx::tmem_ld16(tmem + lane_off + tcol + col0, g);
             ptx::tmem_wait_ld();
@@ -647,8 +662,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // 1. dQ (K buffer) and dV (dS buffer), stored as one bulk group: once it
         // has been read, the next tile's first K and V chunks load there
 #pragma unroll 1
-        for (int pc = 0; pc < kHalfD / 16; ++pc) {
-          const int col0 = half * kHalfD + pc * 16;
+        for (int pc = 0; pc < kPartD / 16; ++pc) {
+          const int col0 = part * kPartD + pc * 16;
           uint32_t gq[16];
           ptx::tmem_ld16(tmem + lane_off + kColDQ + col0, gq);
           ptx::tmem_wait_ld();
@@ -666,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         stage_grad(1);
         ptx::fence_proxy_async_smem();
-        ptx::named_barrier(1, 256);
+        ptx::named_barrier(1, kGradThreads);
         if (gtid == 0) {
           issue_stores(&tm_dq, sm.k);
           issue_stores(&tm_dv, sm.ds);
@@ -681,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::mbar_arrive(&sm.sgrad_free);
         }
         ptx::fence_proxy_async_smem();
-        ptx::named_barrier(1, 256);
+        ptx::named_barrier(1, kGradThreads);
         if (gtid == 0) {
           issue_stores(&tm_dk, sm.p);
           ptx::tma_store_commit();
@@ -782,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D, bool kSplit>
+template <int D, bool kSplit, int kParts>
 int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
            uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   BwdParams p;
@@ -814,12 +829,13 @@ int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorV
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_bwd);
   p.flags_stride = wl.tiles_per_seq;
   const size_t smem = sizeof(BwdSmem<D>) + 1024;
-  if (cudaFuncSetAttribute(bwd_kernel<D, kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
+  auto kern = bwd_kernel<D, kSplit, kParts>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
     return SQB_ERR_LAUNCH;
   const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
-  bwd_kernel<D, kSplit><<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.dout, tm.dq, tm.dk,
-                                                   tm.dv, tm.kbar, tm.vbar, p);
+  kern<<<grid, bwd_threads<kParts>(), smem, stream>>>(tm.q, tm.k, tm.v, tm.o, tm.dout, tm.dq,
+                                                      tm.dk, tm.dv, tm.kbar, tm.vbar, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 
@@ -828,12 +844,13 @@ int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorV
 int launch_backward(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorView o,
                     uint8_t* ws, const WorkspaceLayout& wl, int num_sms, cudaStream_t stream) {
   const bool split = pr.b > 128;
+  constexpr int P = SQB_BWD_PARTS;
   if (pr.D == 64)
-    return split ? launch<64, true>(pr, tm, lse, o, ws, wl, num_sms, stream)
-                 : launch<64, false>(pr, tm, lse, o, ws, wl, num_sms, stream);
+    return split ? launch<64, true, P>(pr, tm, lse, o, ws, wl, num_sms, stream)
+                 : launch<64, false, P>(pr, tm, lse, o, ws, wl, num_sms, stream);
   if (pr.D == 128)
-    return split ? launch<128, true>(pr, tm, lse, o, ws, wl, num_sms, stream)
-                 : launch<128, false>(pr, tm, lse, o, ws, wl, num_sms, stream);
+    return split ? launch<128, true, P>(pr, tm, lse, o, ws, wl, num_sms, stream)
+                 : launch<128, false, P>(pr, tm, lse, o, ws, wl, num_sms, stream);
   return SQB_ERR_UNSUPPORTED;
 }
 

@@ -439,51 +439,79 @@ def reference_attention(q, k, v, scale=None):
 # ---- training caller: fused token cross-entropy (include/sqb_train.h) ------------
 
 
-class _CrossEntropy(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, logits, targets):
-        V = logits.shape[-1]
-        x = logits.reshape(-1, V)
-        if x.stride(-1) != 1 or x.stride(0) < V:
-            x = x.contiguous()
-        t = targets.reshape(-1).to(torch.int64).contiguous()
-        if x.dtype not in _DTYPES or not x.is_cuda or t.numel() != x.shape[0]:
-            raise ValueError("cross_entropy: CUDA float32/bfloat16 logits (..., V) and one "
-                             "target per row")
-        N = x.shape[0]
-        loss = torch.empty(N, dtype=torch.float32, device=x.device)
-        lse = torch.empty(N, dtype=torch.float32, device=x.device)
-        stream = torch.cuda.current_stream(x.device).cuda_stream
-        _lib.check("sqb_xent_fwd", _lib.lib().sqb_xent_fwd(
-            x.data_ptr(), t.data_ptr(), loss.data_ptr(), lse.data_ptr(), N, V, x.stride(0),
-            _DTYPES[x.dtype], stream))
-        counted = (t >= 0).sum().to(torch.float32)
-        ctx.save_for_backward(x, t, lse, counted)
-        ctx.shape = logits.shape
-        return loss.sum() / counted
+@torch.library.custom_op("sqrtblock::xent_fwd", mutates_args=())
+def _xent_fwd(x: torch.Tensor, t: torch.Tensor
+              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Rows x (N, V) (row pitch x.stride(0)), targets t (N,) int64 ->
+    (mean loss over counted rows, per-row log-sum-exp, counted rows)."""
+    N, V = x.shape
+    loss = torch.empty(N, dtype=torch.float32, device=x.device)
+    lse = torch.empty(N, dtype=torch.float32, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    _lib.check("sqb_xent_fwd", _lib.lib().sqb_xent_fwd(
+        x.data_ptr(), t.data_ptr(), loss.data_ptr(), lse.data_ptr(), N, V, x.stride(0),
+        _DTYPES[x.dtype], stream))
+    counted = (t >= 0).sum().to(torch.float32)
+    return loss.sum() / counted, lse, counted
 
-    @staticmethod
-    def backward(ctx, grad):
-        x, t, lse, counted = ctx.saved_tensors
-        scale = (grad.to(torch.float32) / counted).reshape(1).contiguous()
-        N, V = x.shape
-        ld = x.stride(0)
-        # the kernel writes whole rows of the logits' pitch (zeros past V): a full
-        # (N, ld) buffer, of which the first V columns are the gradient
-        dbuf = torch.empty(N, ld, dtype=x.dtype, device=x.device)
-        stream = torch.cuda.current_stream(x.device).cuda_stream
-        _lib.check("sqb_xent_bwd", _lib.lib().sqb_xent_bwd(
-            x.data_ptr(), t.data_ptr(), lse.data_ptr(), scale.data_ptr(), dbuf.data_ptr(), N, V,
-            ld, _DTYPES[x.dtype], stream))
-        return dbuf[:, :V].reshape(ctx.shape), None
+
+@_xent_fwd.register_fake
+def _(x, t):
+    f32 = torch.float32
+    return x.new_empty((), dtype=f32), x.new_empty((x.shape[0],), dtype=f32), \
+        x.new_empty((), dtype=f32)
+
+
+@torch.library.custom_op("sqrtblock::xent_bwd", mutates_args=())
+def _xent_bwd(x: torch.Tensor, t: torch.Tensor, lse: torch.Tensor, scale: torch.Tensor
+              ) -> torch.Tensor:
+    """Gradient rows (N, x.stride(0)) in x's dtype: scale * (softmax - onehot) in
+    the first V columns (zeros past V)."""
+    N, V = x.shape
+    ld = x.stride(0)
+    dbuf = torch.empty(N, ld, dtype=x.dtype, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    _lib.check("sqb_xent_bwd", _lib.lib().sqb_xent_bwd(
+        x.data_ptr(), t.data_ptr(), lse.data_ptr(), scale.data_ptr(), dbuf.data_ptr(), N, V,
+        ld, _DTYPES[x.dtype], stream))
+    return dbuf
+
+
+@_xent_bwd.register_fake
+def _(x, t, lse, scale):
+    return x.new_empty((x.shape[0], x.stride(0)))
+
+
+def _xent_setup(ctx, inputs, output):
+    x, t = inputs
+    _, lse, counted = output
+    ctx.save_for_backward(x, t, lse, counted)
+    ctx.mark_non_differentiable(lse, counted)
+
+
+def _xent_grad(ctx, grad, _dlse, _dcounted):
+    x, t, lse, counted = ctx.saved_tensors
+    scale = (grad.to(torch.float32) / counted).reshape(1).contiguous()
+    return _xent_bwd(x, t, lse, scale)[:, :x.shape[1]], None
+
+
+_xent_fwd.register_autograd(_xent_grad, setup_context=_xent_setup)
 
 
 def cross_entropy(logits, targets):
     """Mean next-token cross-entropy of CUDA logits (..., V) against integer targets
     (negative = ignored), as ``F.cross_entropy`` computes it (fp32 math, mean over
     the counted tokens), fused: the logits are read once forward and the gradient
-    written once backward, in the logits' dtype."""
-    return _CrossEntropy.apply(logits, targets)
+    written once backward, in the logits' dtype (``sqrtblock::xent_fwd/bwd``)."""
+    V = logits.shape[-1]
+    x = logits.reshape(-1, V)
+    if x.stride(-1) != 1 or x.stride(0) < V:
+        x = x.contiguous()
+    t = targets.reshape(-1).to(torch.int64).contiguous()
+    if x.dtype not in _DTYPES or not x.is_cuda or t.numel() != x.shape[0]:
+        raise ValueError("cross_entropy: CUDA float32/bfloat16 logits (..., V) and one "
+                         "target per row")
+    return _xent_fwd(x, t)[0]
 
 
 # ---- training caller: fused LayerNorm (include/sqb_train.h) -----------------------
@@ -497,49 +525,83 @@ def layer_norm_supported(x, weight) -> bool:
             and weight.dtype == torch.float32 and C % 128 == 0 and C <= 1024)
 
 
-class _LayerNorm(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, weight, bias, eps, out_dtype):
-        C = x.shape[-1]
-        x2 = x.reshape(-1, C).contiguous()
-        N = x2.shape[0]
-        y = torch.empty((N, C), dtype=out_dtype, device=x.device)
-        mean = torch.empty(N, dtype=torch.float32, device=x.device)
-        rstd = torch.empty(N, dtype=torch.float32, device=x.device)
-        w = weight.contiguous()
-        b = bias.contiguous() if bias is not None else None
-        stream = torch.cuda.current_stream(x.device).cuda_stream
-        _lib.check("sqb_layernorm_fwd", _lib.lib().sqb_layernorm_fwd(
-            x2.data_ptr(), w.data_ptr(), b.data_ptr() if b is not None else None, y.data_ptr(),
-            _DTYPES[out_dtype], mean.data_ptr(), rstd.data_ptr(), N, C, float(eps), stream))
-        ctx.save_for_backward(x2, w, mean, rstd)
-        ctx.has_bias = b is not None
-        ctx.shape = x.shape
-        return y.view(x.shape)
+@torch.library.custom_op("sqrtblock::layernorm_fwd", mutates_args=())
+def _layernorm_fwd(x2: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], eps: float,
+                   out_dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Rows x2 (N, C) fp32 contiguous -> (y (N, C) in out_dtype, mean, rstd)."""
+    N, C = x2.shape
+    y = torch.empty((N, C), dtype=out_dtype, device=x2.device)
+    mean = torch.empty(N, dtype=torch.float32, device=x2.device)
+    rstd = torch.empty(N, dtype=torch.float32, device=x2.device)
+    stream = torch.cuda.current_stream(x2.device).cuda_stream
+    _lib.check("sqb_layernorm_fwd", _lib.lib().sqb_layernorm_fwd(
+        x2.data_ptr(), w.data_ptr(), b.data_ptr() if b is not None else None, y.data_ptr(),
+        _DTYPES[out_dtype], mean.data_ptr(), rstd.data_ptr(), N, C, float(eps), stream))
+    return y, mean, rstd
 
-    @staticmethod
-    def backward(ctx, dy):
-        x2, w, mean, rstd = ctx.saved_tensors
-        N, C = x2.shape
-        dy2 = dy.reshape(N, C)
-        if dy2.dtype not in _DTYPES:
-            dy2 = dy2.float()
-        dy2 = dy2.contiguous()
-        dx = torch.empty((N, C), dtype=torch.float32, device=x2.device)
-        dw = torch.empty(C, dtype=torch.float32, device=x2.device)
-        db = torch.empty(C, dtype=torch.float32, device=x2.device) if ctx.has_bias else None
-        wsb = _lib.lib().sqb_layernorm_workspace_bytes(N, C)
-        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=x2.device)
-        stream = torch.cuda.current_stream(x2.device).cuda_stream
-        _lib.check("sqb_layernorm_bwd", _lib.lib().sqb_layernorm_bwd(
-            dy2.data_ptr(), _DTYPES[dy2.dtype], x2.data_ptr(), w.data_ptr(), mean.data_ptr(),
-            rstd.data_ptr(), dx.data_ptr(), dw.data_ptr(),
-            db.data_ptr() if db is not None else None, ws.data_ptr(), wsb, N, C, stream))
-        return dx.view(ctx.shape), dw, db, None, None
+
+@_layernorm_fwd.register_fake
+def _(x2, w, b, eps, out_dtype):
+    N, C = x2.shape
+    f32 = torch.float32
+    return (x2.new_empty((N, C), dtype=out_dtype), x2.new_empty((N,), dtype=f32),
+            x2.new_empty((N,), dtype=f32))
+
+
+@torch.library.custom_op("sqrtblock::layernorm_bwd", mutates_args=())
+def _layernorm_bwd(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor, mean: torch.Tensor,
+                   rstd: torch.Tensor, has_bias: bool
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dx (N, C) fp32, dw (C,), db (C,), or an empty db without a bias)."""
+    N, C = x2.shape
+    dx = torch.empty((N, C), dtype=torch.float32, device=x2.device)
+    dw = torch.empty(C, dtype=torch.float32, device=x2.device)
+    db = torch.empty(C if has_bias else 0, dtype=torch.float32, device=x2.device)
+    wsb = _lib.lib().sqb_layernorm_workspace_bytes(N, C)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=x2.device)
+    stream = torch.cuda.current_stream(x2.device).cuda_stream
+    _lib.check("sqb_layernorm_bwd", _lib.lib().sqb_layernorm_bwd(
+        dy2.data_ptr(), _DTYPES[dy2.dtype], x2.data_ptr(), w.data_ptr(), mean.data_ptr(),
+        rstd.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr() if has_bias else None,
+        ws.data_ptr(), wsb, N, C, stream))
+    return dx, dw, db
+
+
+@_layernorm_bwd.register_fake
+def _(dy2, x2, w, mean, rstd, has_bias):
+    N, C = x2.shape
+    f32 = torch.float32
+    return (x2.new_empty((N, C), dtype=f32), x2.new_empty((C,), dtype=f32),
+            x2.new_empty((C if has_bias else 0,), dtype=f32))
+
+
+def _layernorm_setup(ctx, inputs, output):
+    x2, w, b, eps, out_dtype = inputs
+    _, mean, rstd = output
+    ctx.save_for_backward(x2, w, mean, rstd)
+    ctx.has_bias = b is not None
+    ctx.mark_non_differentiable(mean, rstd)
+
+
+def _layernorm_grad(ctx, dy, _dmean, _drstd):
+    x2, w, mean, rstd = ctx.saved_tensors
+    N, C = x2.shape
+    dy2 = dy.reshape(N, C)
+    if dy2.dtype not in _DTYPES:
+        dy2 = dy2.float()
+    dx, dw, db = _layernorm_bwd(dy2.contiguous(), x2, w, mean, rstd, ctx.has_bias)
+    return dx, dw, (db if ctx.has_bias else None), None, None
+
+
+_layernorm_fwd.register_autograd(_layernorm_grad, setup_context=_layernorm_setup)
 
 
 def layer_norm(x, weight, bias=None, eps=1e-5, out_dtype=torch.float32):
     """LayerNorm over the last dimension of CUDA fp32 ``x`` (see
     ``layer_norm_supported``), fp32 math; the output in ``out_dtype`` (fp32, or
-    bf16 for a bf16 autocast consumer, which would cast it to that anyway)."""
-    return _LayerNorm.apply(x, weight, bias, eps, out_dtype)
+    bf16 for a bf16 autocast consumer, which would cast it to that anyway).
+    The ``sqrtblock::layernorm_fwd/bwd`` custom ops."""
+    C = x.shape[-1]
+    x2 = x.reshape(-1, C).contiguous()
+    b = bias.contiguous() if bias is not None else None
+    return _layernorm_fwd(x2, weight.contiguous(), b, float(eps), out_dtype)[0].view(x.shape)

@@ -14,6 +14,7 @@ seeded generator: no dataset is involved.
 from __future__ import annotations
 
 import inspect
+from contextlib import nullcontext
 
 import torch
 import torch.nn.functional as F
@@ -73,18 +74,46 @@ class Trainer:
                                               device_type=device.type)
         self.autocast = autocast and device.type == "cuda"
 
-    def step(self, x, y):
+    def step(self, x, y, report=None):
         """One optimizer step.  First raises if an attention kernel of an earlier
         step posted a device-side failure (a non-blocking check of the
-        library's page-locked mailboxes: that step's gradients were invalid)."""
+        library's page-locked mailboxes: that step's gradients were invalid).
+        ``report`` (a ``metrics.MetricsReport``) times the forward, backward and
+        optimizer phases as the reference trainer does (train.py:488-505)."""
         if self.device.type == "cuda":
             check_status(self.device)
+        span = report.phase if report is not None else (lambda _label: nullcontext())
         self.optimizer.zero_grad(set_to_none=True)
-        with torch.autocast(device_type=self.device.type, dtype=torch.bfloat16,
-                            enabled=self.autocast):
+        with span("forward"), torch.autocast(device_type=self.device.type,
+                                             dtype=torch.bfloat16, enabled=self.autocast):
             logits = self.model(x, pad_vocab=True)
             loss = calculate_loss(logits, y)
-        loss.backward()
-        norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), 1.0)
-        self.optimizer.step()
+        with span("backward"):
+            loss.backward()
+        with span("optimizer"):
+            norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), 1.0)
+            self.optimizer.step()
         return loss.detach(), norm
+
+    def run_info(self, config, batch, seq, max_steps, lr, seed, compiled=False):
+        """The ``run`` section of a metrics.json report (the reference's keys,
+        train.py's run description): device, model and training settings."""
+        raw = self.raw_model
+        n = sum(p.numel() for p in raw.parameters())
+        emb = raw.transformer.wpe.weight.numel()
+        dev = self.device
+        return {
+            "device": dev.type,
+            "gpu_name": torch.cuda.get_device_name(dev) if dev.type == "cuda" else None,
+            "torch_version": torch.__version__,
+            "autocast_dtype": "bfloat16" if self.autocast else None,
+            "torch_compile": compiled, "attention_profiling": True,
+            "attention": config.attention, "seed": seed, "num_parameters": n,
+            "num_parameters_non_embedding": n - emb,
+            "model_config": {k: getattr(config, k) for k in (
+                "block_size", "vocab_size", "n_layer", "n_head", "n_embd", "dropout", "bias",
+                "attention")},
+            "batch_size": batch, "seq_len": seq, "grad_accumulation_steps": 1,
+            "max_steps": max_steps, "max_lr": lr, "min_lr": lr, "warmup_steps": 0,
+            "eval_interval": 0, "eval_iters": 0, "data_dir": "synthetic (uniform token ids)",
+        }

@@ -1,7 +1,7 @@
-"""Generate the golden fixtures under tests/golden/.  Run in a container that has
-the reference checkout at /root/reference (it is read, never modified):
+"""Generate the golden fixtures under tests/golden/.  Run where a checkout of the
+reference repository is available (it is read, never modified):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference PATH_TO_REFERENCE_CHECKOUT
 
 Fixtures written:
 
@@ -21,6 +21,10 @@ Fixtures written:
   its Wq/Wk/Wv replaced by modules returning seeded leaf tensors Q, K, V and
   c_proj the identity, so the stored output and dQ/dK/dV are the core's.  They
   pin oracle/refsem_oracle.py and the CUDA reference-semantics mode.
+* ``ref_metrics_schema.json`` - the key paths of the reference trainer's
+  ``metrics.json`` (metrics.py:516-537: run / aggregates / train / val / _stats),
+  read from the run it ships (vanilla/metrics.json); the training report of
+  this repository writes the same schema.
 * ``oracle_T200.npz`` - a frozen forward/backward of the oracle itself on a
   ragged case (T=200, b=16: 12 complete blocks and a partial block of 8), so
   any later change to the oracle shows up as a fixture mismatch.
@@ -117,7 +121,8 @@ def _reference_full(ref_root, B, H, T, D, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="path of the reference checkout (read only)")
     args = ap.parse_args()
     sys.path.insert(0, REPO)
     from oracle import sqrtblock_oracle as orc
@@ -194,6 +199,23 @@ def main():
                             dq=dq.astype(np.float32), dk=dk.astype(np.float32),
                             dv=dv.astype(np.float32))
         print(f"wrote {path}: max|oracle - reference| = {err:.3e}")
+
+    # key paths of the reference's metrics.json ("[]" marks a list's rows)
+    def paths(x, prefix=""):
+        if isinstance(x, dict):
+            for k, v in x.items():
+                yield f"{prefix}/{k}"
+                yield from paths(v, f"{prefix}/{k}")
+        elif isinstance(x, list) and x:
+            yield from paths(x[0], f"{prefix}[]")
+
+    with open(os.path.join(args.reference, "vanilla", "metrics.json")) as f:
+        recorded = json.load(f)
+    path = os.path.join(HERE, "ref_metrics_schema.json")
+    with open(path, "w") as f:
+        json.dump({"source": "vanilla/metrics.json of the reference",
+                   "paths": sorted(set(paths(recorded)))}, f, indent=1)
+    print(f"wrote {path}")
 
     B, H, T, D, b = 1, 2, 200, 32, 16
     rng = np.random.default_rng(3)

@@ -164,3 +164,54 @@ def test_gpu_fused_caller_ops_match_torch_ops_end_to_end(monkeypatch):
         cos = float(torch.dot(a, b) / (a.norm() * b.norm() + 1e-30))
         assert cos > 0.999, (n, cos)
         assert float((a.norm() - b.norm()).abs() / (b.norm() + 1e-30)) < 1e-2, n
+
+
+def test_metrics_report_has_the_reference_schema(tmp_path):
+    """A CPU run written by MetricsReport has every key path of the reference's
+    metrics.json (tests/golden/ref_metrics_schema.json, read from the run the
+    reference ships), and the warm-up steps are excluded from the means."""
+    import json
+
+    from llm_training_b200.metrics import MetricsReport
+    from llm_training_b200.model.attention_registry import BaseAttention
+
+    cfg = tiny()
+    tr = Trainer(cfg, torch.device("cpu"), lr=3e-3, seed=0)
+    gen = torch.Generator().manual_seed(0)
+    x, y = synthetic_batch(gen, 2, 32, 97, torch.device("cpu"))
+    path = str(tmp_path / "metrics.json")
+    info = tr.run_info(cfg, 2, 32, max_steps=6, lr=3e-3, seed=0)
+    rep = MetricsReport(path, info, tokens_per_step=64, warmup_steps_skipped=2, log_interval=2,
+                        device_type="cpu")
+    assert rep.attach_attention(tr.raw_model, BaseAttention) == cfg.n_layer
+    for step in range(6):
+        rep.begin_step(step)
+        loss, norm = tr.step(x, y, report=rep)
+        rep.end_step(step, float(loss), 3e-3, float(norm))
+    rep.log_validation(6, 4.0)
+    rep.write("finished")
+    doc = json.load(open(path))
+
+    def paths(d, prefix=""):
+        if isinstance(d, dict):
+            for k, v in d.items():
+                yield f"{prefix}/{k}"
+                yield from paths(v, f"{prefix}/{k}")
+        elif isinstance(d, list) and d:
+            yield from paths(d[0], f"{prefix}[]")
+
+    ref = json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                      "ref_metrics_schema.json")))["paths"]
+    # the reference's CPU-less keys (peak memory) and the resume breadcrumb
+    # appear only on CUDA runs / resumed runs; its phases include "data"
+    optional = ("/run/resumed_at", "/aggregates/avg_peak_memory_mib",
+                "/aggregates/attention/peak_memory_mib", "/_stats/phase_time/data")
+    missing = [p for p in ref if p not in set(paths(doc)) and not p.startswith(optional)]
+    assert missing == []
+    agg = doc["aggregates"]
+    assert agg["measured_steps"] == 4                      # steps 2..5
+    assert doc["_stats"]["step_time"]["count"] == 4
+    assert [r["step"] for r in doc["train"]] == [0, 2, 4, 5]
+    assert agg["attention"]["layers"] == cfg.n_layer
+    assert 0 < agg["attention"]["fraction_of_step_time"] < 1
+    assert doc["run"]["status"] == "finished"
