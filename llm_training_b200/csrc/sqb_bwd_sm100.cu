@@ -334,11 +334,13 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
           if (kTransposedSums && c < t.nsc) {
             // summary gradients transposed (D = 128 = M): all 128 columns of
             // P / dS, zero outside the chunk's visible summaries
+            // N = the chunk's n16 summary columns: only what the drain reads
+            const uint32_t idesc_sum = ptx::idesc_bf16(128, N, true, true);
             for (int kk = 0; kk < kq; ++kk)  // dVc^T = dO^T P
-              ptx::mma_ss(tmem + kColS, desc_mnmajor(do_s, kk), desc_mnmajor(p_s, kk), idesc_dvdk,
+              ptx::mma_ss(tmem + kColS, desc_mnmajor(do_s, kk), desc_mnmajor(p_s, kk), idesc_sum,
                           kk > 0 ? 1u : 0u);
             for (int kk = 0; kk < kq; ++kk)  // dKc^T = Q^T dS
-              ptx::mma_ss(tmem + kColDP, desc_mnmajor(q_s, kk), desc_mnmajor(ds_s, kk), idesc_dvdk,
+              ptx::mma_ss(tmem + kColDP, desc_mnmajor(q_s, kk), desc_mnmajor(ds_s, kk), idesc_sum,
                           kk > 0 ? 1u : 0u);
           } else {
             for (int kk = 0; kk < kq; ++kk)  // dVc = P^T dO
@@ -387,7 +389,10 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
       const int tq = t.r0 + row;
       const int blk_t = valid ? tq / p.g.b : 0;
       const int lim = valid ? min(blk_t, p.g.Gc) : 0;
-      const float L = valid ? p.lse[(size_t)t.bh * p.g.T + tq] * kLog2e : 0.f;
+      // The row's LSE is loaded here and first used after the delta barrier:
+      // a warp issues in order and would otherwise stall on this global load
+      // (a few thousand cycles under load) before computing delta.
+      float L = valid ? __ldg(p.lse + (size_t)t.bh * p.g.T + tq) : 0.f;
       // delta = rowsum(dO * O); O was loaded into the V buffer.  Each part sums
       // its D/kParts columns; the parts meet in shared memory.
       float dpart_sum = 0.f;
@@ -411,6 +416,8 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
       // chunk may be loaded.
       ptx::named_barrier(1, kGradThreads);
       if (gtid == 0) ptx::mbar_arrive(&sm.delta_done);
+      ptx::reg_fence1(L);  // first use of the LSE load: after delta
+      L *= kLog2e;
       float delta = sm.dpart[0][row];
 #pragma unroll
       for (int i = 1; i < kParts; ++i) delta += sm.dpart[i][row];
@@ -426,7 +433,11 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         const float delta_s = delta * p.scale;
         // this part's 16-column pieces; a piece is live (warp-uniform) when it
         // holds a column some row of this warp sees
-        auto col0 = [&](int pi) { return (part * kPieces + pi) * 16; };
+        // pieces of the parts interleave (piece pi of part h covers columns
+        // 16 * (pi * kParts + h)), so a chunk with few live columns - a summary
+        // chunk of few summaries, the causal chunk's lower lane quarters -
+        // still splits them between the parts
+        auto col0 = [&](int pi) { return (pi * kParts + part) * 16; };
         auto live = [&](int pi) {
           const int c0 = col0(pi);
           return c0 < N && c0 < whi && c0 + 16 > wlo;
@@ -539,7 +550,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         float* dkb = p.dkbar + (size_t)t.bh * p.g.Gc * D + row;
 #pragma unroll 1
         for (int pc = 0; pc < kPieces; ++pc) {
-          const int col0 = (part * kPieces + pc) * 16;
+          const int col0 = (pc * kParts + part) * 16;  // interleaved as in softmax_grad
           if (col0 + 16 <= clo || col0 >= chi) continue;  // warp-uniform
           uint32_t gv[16], gk[16];
           ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);

@@ -382,6 +382,10 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
                  "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7]));
 }
 
+// Opaque redefinition of one register: code after it that uses `x` cannot be
+// moved above it, so a pending load into `x` is waited for here, not earlier.
+__device__ __forceinline__ void reg_fence1(float& x) { asm volatile("" : "+f"(x)); }
+
 // 32 lanes x 16 consecutive 32-bit columns -> 16 registers per thread.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
