@@ -22,6 +22,8 @@ Default workload (attn-t16k), one JSON line:
     N > 1; with the same steps run without the all-reduce, and a flat
     all-reduce of the gradients' size timed alone, to show how much of the
     collective the backward hides.
+  * ``train_gpt2_medium_8k``: the same for GPT-2 medium (24L/16H/1024) at
+    T=8192 (b=96), 8 sequences per rank.
 Multi-GPU: one process per GPU under torchrun; every rank runs its own 16
 heads for the top-level metric (weak scaling; the (batch, head) units are
 independent, so there is no data-path collective).
@@ -470,6 +472,10 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
         extra["train"] = train_record(args, "gpt2-small", world, rank, local,
                                       args.train_steps, args.train_warmup)
+        if not args.no_train_medium:
+            torch.cuda.empty_cache()
+            extra["train_gpt2_medium_8k"] = train_record(
+                args, "gpt2-medium-8k", world, rank, local, max(args.train_steps // 3, 5), 3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -706,7 +712,7 @@ def train_record(args, workload, world, rank, local, steps, warmup):
             for _ in range(2)]
     torch.cuda.synchronize()
     barrier(world)
-    e_steps = max(steps, 20)
+    e_steps = max(steps, 10)
     e0 = time.perf_counter()
     for i in range(e_steps):
         tok = host[i % 2].to(dev, non_blocking=True)
@@ -774,6 +780,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-train", action="store_true", help="skip the train sub-record")
     ap.add_argument("--no-h64", action="store_true", help="skip the h64_split sub-record")
+    ap.add_argument("--no-train-medium", action="store_true",
+                    help="skip the GPT-2 medium T=8K training sub-record")
     ap.add_argument("--train-steps", type=int, default=30)
     ap.add_argument("--train-warmup", type=int, default=5)
     ap.add_argument("--h64-steps", type=int, default=30)

@@ -53,13 +53,20 @@ __device__ __forceinline__ E* at_w(const TensorView& t, int n, int tok, int h) {
          (int64_t)h * t.sh;
 }
 
-// Block i's L x D rows of a (B, T, H, D) view into shared memory as fp32.
+// Row pitch of the L x D fp32 tiles in shared memory: D + 1, so that a warp
+// whose lanes read the same column d of 32 different rows (the q.k and dP.v
+// products, lanes along the key index) hits 32 different banks; with a pitch
+// of D (a multiple of 32) all 32 lanes hit one bank.
+__host__ __device__ __forceinline__ int tile_pitch(int D) { return D + 1; }
+
+// Block i's L x D rows of a (B, T, H, D) view into shared memory as fp32, rows
+// ld floats apart (the padded pitch unless a kernel reads the tile along rows only).
 template <typename E>
 __device__ void load_tile(float* dst, const TensorView& t, int n, int h, int i,
-                          const RefsemParams& p) {
+                          const RefsemParams& p, int ld) {
   for (int e = threadIdx.x; e < p.L * p.D; e += kThreads) {
     const int l = e / p.D, d = e % p.D;
-    dst[e] = ld_f(at<E>(t, n, i * p.L + l, h) + d);
+    dst[l * ld + d] = ld_f(at<E>(t, n, i * p.L + l, h) + d);
   }
 }
 
@@ -77,12 +84,12 @@ __device__ __forceinline__ float warp_max(float x) {
 // local = causal softmax(q k^T * scale) of one block, L x L in shared memory
 // (zero above the diagonal).  q, k: L x D fp32 tiles.
 __device__ void local_map(float* local, const float* q, const float* k, const RefsemParams& p) {
-  const int L = p.L, D = p.D;
+  const int L = p.L, D = p.D, ld = tile_pitch(D);
   for (int e = threadIdx.x; e < L * L; e += kThreads) {
     const int l = e / L, m = e % L;
     float s = 0.f;
     if (m <= l) {
-      for (int d = 0; d < D; ++d) s += q[l * D + d] * k[m * D + d];
+      for (int d = 0; d < D; ++d) s += q[l * ld + d] * k[m * ld + d];
       s *= p.scale;
     }
     local[e] = s;
@@ -112,14 +119,14 @@ __global__ void __launch_bounds__(kThreads) local_summary_p_kernel(
     TensorView q, TensorView k, TensorView v, float* summary, float* P, RefsemParams p) {
   extern __shared__ float sm[];
   const int i = blockIdx.x, bh = blockIdx.y, n = bh / p.H, h = bh % p.H;
-  const int L = p.L, D = p.D;
+  const int L = p.L, D = p.D, ld = tile_pitch(D);
   float* sq = sm;
-  float* sk = sq + L * D;
-  float* sv = sk + L * D;
-  float* local = sv + L * D;
-  load_tile<E>(sq, q, n, h, i, p);
-  load_tile<E>(sk, k, n, h, i, p);
-  load_tile<E>(sv, v, n, h, i, p);
+  float* sk = sq + L * ld;
+  float* sv = sk + L * ld;
+  float* local = sv + L * ld;
+  load_tile<E>(sq, q, n, h, i, p, ld);
+  load_tile<E>(sk, k, n, h, i, p, ld);
+  load_tile<E>(sv, v, n, h, i, p, ld);
   __syncthreads();
   local_map(local, sq, sk, p);
   if (summary) {
@@ -133,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) local_summary_p_kernel(
   for (int e = threadIdx.x; e < L * D; e += kThreads) {
     const int l = e / D, d = e % D;
     float acc = 0.f;
-    for (int m = 0; m <= l; ++m) acc += local[l * L + m] * sv[m * D + d];
+    for (int m = 0; m <= l; ++m) acc += local[l * L + m] * sv[m * ld + d];
     Pi[e] = acc;
   }
 }
@@ -196,9 +203,8 @@ __global__ void __launch_bounds__(kThreads) dp_dglob_kernel(TensorView dout, con
   extern __shared__ float sm[];
   const int j = blockIdx.x, bh = blockIdx.y, n = bh / p.H, h = bh % p.H;
   const int L = p.L, D = p.D, G = p.G;
-  float* sdo = sm;        // dO_j, L x D
-  float* red = sdo + L * D;  // kThreads / 32 partial sums
-  load_tile<E>(sdo, dout, n, h, j, p);
+  float* sdo = sm;  // dO_j, L x D, contiguous (read along rows only)
+  load_tile<E>(sdo, dout, n, h, j, p, D);
   __syncthreads();
   const float* gb = glob + (size_t)bh * G * G;
   float* dPj = dP + ((size_t)bh * G + j) * L * D;
@@ -211,20 +217,15 @@ __global__ void __launch_bounds__(kThreads) dp_dglob_kernel(TensorView dout, con
   const float* Pb = P + (size_t)bh * G * L * D;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* dg = dglob + ((size_t)bh * G + j) * G;
-  for (int c = 0; c < G; ++c) {
+  // one warp per earlier block c: d_glob[j, c] = <dO_j, P_c>, zero for c >= j
+  for (int c = warp; c < j; c += kThreads / 32) {
+    const float* Pc = Pb + (size_t)c * L * D;
     float part = 0.f;
-    if (c < j)
-      for (int e = threadIdx.x; e < L * D; e += kThreads) part += sdo[e] * Pb[(size_t)c * L * D + e];
+    for (int e = lane; e < L * D; e += 32) part += sdo[e] * Pc[e];
     part = warp_sum(part);
-    if (lane == 0) red[warp] = part;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float s = 0.f;
-      for (int w = 0; w < kThreads / 32; ++w) s += red[w];
-      dg[c] = s;
-    }
-    __syncthreads();
+    if (lane == 0) dg[c] = part;
   }
+  for (int c = j + threadIdx.x; c < G; c += kThreads) dg[c] = 0.f;
 }
 
 // Per bh: d_gs = glob * (d_glob - rowsum(glob * d_glob)); d_summary =
@@ -267,18 +268,18 @@ __global__ void __launch_bounds__(kThreads) local_grads_kernel(
     TensorView dq, TensorView dk, TensorView dv, RefsemParams p) {
   extern __shared__ float sm[];
   const int i = blockIdx.x, bh = blockIdx.y, n = bh / p.H, h = bh % p.H;
-  const int L = p.L, D = p.D;
+  const int L = p.L, D = p.D, ld = tile_pitch(D);
   float* sq = sm;
-  float* sk = sq + L * D;
-  float* sv = sk + L * D;
-  float* sdp = sv + L * D;
-  float* local = sdp + L * D;
+  float* sk = sq + L * ld;
+  float* sv = sk + L * ld;
+  float* sdp = sv + L * ld;
+  float* local = sdp + L * ld;
   float* ds = local + L * L;
-  load_tile<E>(sq, q, n, h, i, p);
-  load_tile<E>(sk, k, n, h, i, p);
-  load_tile<E>(sv, v, n, h, i, p);
+  load_tile<E>(sq, q, n, h, i, p, ld);
+  load_tile<E>(sk, k, n, h, i, p, ld);
+  load_tile<E>(sv, v, n, h, i, p, ld);
   const float* dPi = dP + ((size_t)bh * p.G + i) * L * D;
-  for (int e = threadIdx.x; e < L * D; e += kThreads) sdp[e] = dPi[e];
+  for (int e = threadIdx.x; e < L * D; e += kThreads) sdp[(e / D) * ld + e % D] = dPi[e];
   __syncthreads();
   local_map(local, sq, sk, p);
   const float* dsi = dsum + ((size_t)bh * p.G + i) * L;
@@ -286,7 +287,7 @@ __global__ void __launch_bounds__(kThreads) local_grads_kernel(
     const int l = e / L, m = e % L;
     float g = 0.f;
     if (m <= l) {
-      for (int d = 0; d < D; ++d) g += sdp[l * D + d] * sv[m * D + d];
+      for (int d = 0; d < D; ++d) g += sdp[l * ld + d] * sv[m * ld + d];
       g += dsi[m];
     }
     ds[e] = g;  // d_local for now
@@ -304,10 +305,10 @@ __global__ void __launch_bounds__(kThreads) local_grads_kernel(
   for (int e = threadIdx.x; e < L * D; e += kThreads) {
     const int r = e / D, d = e % D;
     float gq = 0.f, gk = 0.f, gv = 0.f;
-    for (int m = 0; m <= r; ++m) gq += ds[r * L + m] * sk[m * D + d];  // row r as query
-    for (int l = r; l < L; ++l) {                                      // row r as key
-      gk += ds[l * L + r] * sq[l * D + d];
-      gv += local[l * L + r] * sdp[l * D + d];
+    for (int m = 0; m <= r; ++m) gq += ds[r * L + m] * sk[m * ld + d];  // row r as query
+    for (int l = r; l < L; ++l) {                                       // row r as key
+      gk += ds[l * L + r] * sq[l * ld + d];
+      gv += local[l * L + r] * sdp[l * ld + d];
     }
     st_f(at_w<E>(dq, n, i * L + r, h) + d, gq * p.scale);
     st_f(at_w<E>(dk, n, i * L + r, h) + d, gk * p.scale);
@@ -367,7 +368,7 @@ int refsem_forward(TensorView q, TensorView k, TensorView v, TensorView o, float
                    float* summary, uint8_t* ws, const RefsemWorkspace& wl, int BH,
                    const RefsemParams& p, cudaStream_t s) {
   float* P = reinterpret_cast<float*>(ws + wl.P);
-  const size_t sm1 = (size_t)(3 * p.L * p.D + p.L * p.L) * 4;
+  const size_t sm1 = (size_t)(3 * p.L * tile_pitch(p.D) + p.L * p.L) * 4;
   const size_t sm2 = (size_t)(p.G * p.L + p.G * p.G) * 4;
   if (!set_smem(local_summary_p_kernel<E>, sm1) || !set_smem(glob_kernel, sm2))
     return SQB_ERR_LAUNCH;
@@ -386,10 +387,10 @@ int refsem_backward(TensorView q, TensorView k, TensorView v, TensorView dout, c
   float* dP = reinterpret_cast<float*>(ws + wl.dP);
   float* dglob = reinterpret_cast<float*>(ws + wl.dglob);
   float* dsum = reinterpret_cast<float*>(ws + wl.dsum);
-  const size_t sm1 = (size_t)(3 * p.L * p.D + p.L * p.L) * 4;
-  const size_t sm2 = (size_t)(p.L * p.D + kThreads / 32) * 4;
+  const size_t sm1 = (size_t)(3 * p.L * tile_pitch(p.D) + p.L * p.L) * 4;
+  const size_t sm2 = (size_t)(p.L * p.D) * 4;
   const size_t sm3 = (size_t)(p.G * p.G + p.G * p.L) * 4;
-  const size_t sm4 = (size_t)(4 * p.L * p.D + 2 * p.L * p.L) * 4;
+  const size_t sm4 = (size_t)(4 * p.L * tile_pitch(p.D) + 2 * p.L * p.L) * 4;
   if (!set_smem(local_summary_p_kernel<E>, sm1) || !set_smem(dp_dglob_kernel<E>, sm2) ||
       !set_smem(dglob_dsummary_kernel, sm3) || !set_smem(local_grads_kernel<E>, sm4))
     return SQB_ERR_LAUNCH;
