@@ -70,8 +70,25 @@ struct BwdParams {
   int store_rows;  // rows per dQ/dK/dV store box
 };
 
+// At D = 64 with b <= 128 shared memory has room for the tile's own keys and
+// values (its in-block chunk) in buffers of their own, so the in-block S and dP
+// never wait for a K / V load behind the summary chunk's MMAs.  The epilogue
+// then stages dQ and dV there (instead of in the K and dS buffers), so the
+// next tile's summary Kbar / Vbar load as soon as it is claimed.
+template <int D, bool kSplit>
+constexpr bool in_bufs() {
+  return D == 64 && !kSplit;
+}
+template <int D, bool kIn>
+struct BwdInBufs {};
 template <int D>
-struct BwdSmem {
+struct BwdInBufs<D, true> {
+  alignas(1024) uint8_t kin[(D / 64) * kAtomBytes];
+  alignas(1024) uint8_t vin[(D / 64) * kAtomBytes];
+};
+
+template <int D, bool kIn>
+struct BwdSmem : BwdInBufs<D, kIn> {
   static constexpr int kTileBytes = (D / 64) * kAtomBytes;
   alignas(1024) uint8_t q[kTileBytes];     // Q
   alignas(1024) uint8_t dout[kTileBytes];  // dO
@@ -88,6 +105,7 @@ struct BwdSmem {
   uint64_t red_done, pub_read, sums_ready, sgrad_free;
   uint64_t mma_done;  // exit: every MMA of the CTA has completed
   uint64_t dq_full;   // the tile's dQ accumulation is complete
+  uint64_t in_full;   // the in-block K / V buffers have landed (in_bufs)
   int tile_ring;
   uint32_t tmem_base;
 };
@@ -118,7 +136,8 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
                const __grid_constant__ CUtensorMap tm_kbar,
                const __grid_constant__ CUtensorMap tm_vbar, const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
-  BwdSmem<D>& sm = *reinterpret_cast<BwdSmem<D>*>(
+  constexpr bool kIn = in_bufs<D, kSplit>();
+  BwdSmem<D, kIn>& sm = *reinterpret_cast<BwdSmem<D, kIn>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -151,6 +170,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
     ptx::mbar_init(&sm.g_free, kGradWarps);
     ptx::mbar_init(&sm.mma_done, 1);
     ptx::mbar_init(&sm.dq_full, 1);
+    ptx::mbar_init(&sm.in_full, 1);
     ptx::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -187,7 +207,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         const int c = (int)atomicAdd(p.ctrl + kBwdTileCounter, 1u);
         return c < p.total_tiles ? c : -1;
       };
-      int tc = 0, kc = 0;
+      int tc = 0, kc = 0;  // kc: chunks loaded through the K / V buffers
       while (true) {
         if (tc > 0) {
           ptx::mbar_wait(&sm.ld_empty, (tc - 1) & 1, status, 0x50000000u);
@@ -204,6 +224,9 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
           // the copies issued so far have landed (they normally have: after a
           // failed wait they may still be in flight)
           if (tc > 0) ptx::mbar_drain(&sm.ld_full, (tc - 1) & 1);
+          if constexpr (kIn) {
+            if (tc > 0) ptx::mbar_drain(&sm.in_full, (tc - 1) & 1);
+          }
           if (kc > 0) {
             ptx::mbar_drain(&sm.k_full, (kc - 1) & 1);
             ptx::mbar_drain(&sm.v_full, (kc - 1) & 1);
@@ -231,9 +254,10 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         // the first chunk loaded into the V buffer waits for delta (O is there)
         const int first_v = t.nsc > 0 ? 1 : 0;
         for (int c = 0; c < nch; ++c) {
+          if (kIn && c == t.nsc) continue;  // the in-block chunk, loaded above
           auto load_k = [&]() {
             ptx::mbar_wait(&sm.k_empty, (kc & 1) ^ 1, status, 0x51000000u);
-            if (c == 0 && tc > 0)
+            if (!kIn && c == 0 && tc > 0)
               ptx::mbar_wait(&sm.stage_free, (tc - 1) & 1, status, 0x54000000u);
             if (c < t.nsc) {
               const SumChunk sc = sum_chunk(t, c);
@@ -255,7 +279,11 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
             if (c == first_v) ptx::mbar_wait(&sm.delta_done, tc & 1, status, 0x52000000u);
             if (c < t.nsc) {
               // chunk 0 into the dS buffer, free since the previous tile's
-              // staging was read (stage_free, waited for by load_k above)
+              // staging was read (stage_free, waited for by load_k above), or
+              // with in-block buffers (no staging there) once its last MMA
+              // has read its dS
+              if (kIn && c == 0 && tc > 0)
+                ptx::mbar_wait(&sm.dq_full, (tc - 1) & 1, status, 0x57000000u);
               const SumChunk sc = sum_chunk(t, c);
               uint8_t* dst = c == 0 ? sm.ds : sm.v;
               ptx::mbar_arrive_expect_tx(&sm.v_full, kAtoms * kAtomBytes);
@@ -284,6 +312,19 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
           }
           ++kc;
         }
+        if constexpr (kIn) {
+          // the tile's own keys and values, needed last: once the previous
+          // tile's dQ / dV staging there has been read by its TMA stores
+          if (tc > 0) ptx::mbar_wait(&sm.stage_free, (tc - 1) & 1, status, 0x54000000u);
+          ptx::mbar_arrive_expect_tx(&sm.in_full, 2 * kAtoms * box_bytes);
+#pragma unroll
+          for (int a = 0; a < kAtoms; ++a) {
+            ptx::tma_load_4d(sm.kin + a * kAtomBytes, &tm_k, &sm.in_full, a * 64, t.h, t.r0,
+                             t.n);
+            ptx::tma_load_4d(sm.vin + a * kAtomBytes, &tm_v, &sm.in_full, a * 64, t.h, t.r0,
+                             t.n);
+          }
+        }
         ++tc;
       }
     }
@@ -295,7 +336,12 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
       const uint32_t q_s = ptx::smem_u32(sm.q), do_s = ptx::smem_u32(sm.dout);
       const uint32_t k_s = ptx::smem_u32(sm.k), v_s = ptx::smem_u32(sm.v);
       const uint32_t p_s = ptx::smem_u32(sm.p), ds_s = ptx::smem_u32(sm.ds);
-      int tc = 0, kc = 0;
+      uint32_t kin_s = 0, vin_s = 0;
+      if constexpr (kIn) {
+        kin_s = ptx::smem_u32(sm.kin);
+        vin_s = ptx::smem_u32(sm.vin);
+      }
+      int tc = 0, kc = 0, kv = 0;  // kv: chunks read from the K / V buffers
       while (true) {
         ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x60000000u);
         const int n = sm.tile_ring;
@@ -309,25 +355,31 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
           // the previous chunk's gradients to be read (g_free)
           const bool late_last = c > 0 && c == nch - 1;
           const uint32_t col_s = c == nch - 1 ? kColSLast : kColS;
-          ptx::mbar_wait(&sm.k_full, kc & 1, status, 0x61000000u);
+          const bool inb = kIn && c == t.nsc;  // K / V in the in-block buffers
+          const uint32_t kc_s = inb ? kin_s : k_s;
+          if (inb)
+            ptx::mbar_wait(&sm.in_full, tc & 1, status, 0x65000000u);
+          else
+            ptx::mbar_wait(&sm.k_full, kv & 1, status, 0x61000000u);
           if (kc > 0 && !late_last)
             ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
           ptx::tc_fence_after();
           const uint32_t idesc_s = ptx::idesc_bf16(128, N, false, false);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            ptx::mma_ss(tmem + col_s, desc_kmajor(q_s, kk), desc_kmajor(k_s, kk), idesc_s,
+            ptx::mma_ss(tmem + col_s, desc_kmajor(q_s, kk), desc_kmajor(kc_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
-          ptx::mbar_wait(&sm.v_full, kc & 1, status, 0x64000000u);
+          if (!inb) ptx::mbar_wait(&sm.v_full, kv & 1, status, 0x64000000u);
           if (late_last) ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
           ptx::tc_fence_after();
-          const uint32_t vc_s = (c == 0 && t.nsc > 0) ? ds_s : v_s;  // where this chunk's V is
+          // where this chunk's V is
+          const uint32_t vc_s = inb ? vin_s : (c == 0 && t.nsc > 0) ? ds_s : v_s;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             ptx::mma_ss(tmem + kColDP, desc_kmajor(do_s, kk), desc_kmajor(vc_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
           ptx::mma_commit(&sm.s_full);
-          ptx::mma_commit(&sm.v_empty);  // the V chunk is read only by dP
+          if (!inb) ptx::mma_commit(&sm.v_empty);  // the V chunk is read only by dP
           ptx::mbar_wait(&sm.ps_full, kc & 1, status, 0x63000000u);
           ptx::tc_fence_after();
           // dVc / dKc first: their drain (or the epilogue) starts while dQ runs
@@ -353,11 +405,12 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
           ptx::mma_commit(&sm.g_full);
           if (c == nch - 1) ptx::mma_commit(&sm.ld_empty);  // Q, dO, V no longer read
           for (int kk = 0; kk < N / 16; ++kk)  // dQ += dS Kc
-            ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(k_s, kk), idesc_dq,
+            ptx::mma_ss(tmem + kColDQ, desc_kmajor(ds_s, kk), desc_mnmajor(kc_s, kk), idesc_dq,
                         (c > 0 || kk > 0) ? 1u : 0u);
-          ptx::mma_commit(&sm.k_empty);
+          if (!inb) ptx::mma_commit(&sm.k_empty);
           if (c == nch - 1) ptx::mma_commit(&sm.dq_full);
           ++kc;
+          if (!inb) ++kv;
         }
         ++tc;
       }
@@ -448,11 +501,23 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
             ptx::tmem_ld16(tmem + lane_off + kColDP + col0(pi), dp);
           }
         };
-        // P = exp2(S*c - L), dS = P * (dP*scale - delta*scale); masked -> 0
+        // P = exp2(S*c - L), dS = P * (dP*scale - delta*scale); masked -> 0.
+        // A piece no row of the warp sees only gets its zeros (warp-uniform):
+        // the MMAs read every column, and its exponentials would be discarded.
         auto emit = [&](int pi, const uint32_t (&sv)[16], const uint32_t (&dp)[16]) {
           const int c0 = col0(pi);
           const bool lv = live(pi);
-          const bool whole = lv && c0 >= lo_max && c0 + 16 <= hi_min;
+          if (!lv) {
+            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int j8 = 0; j8 < 2; ++j8) {
+              const uint32_t off = swz_offset(row, c0 + j8 * 8);
+              *reinterpret_cast<uint4*>(sm.p + off) = z;
+              *reinterpret_cast<uint4*>(sm.ds + off) = z;
+            }
+            return;
+          }
+          const bool whole = c0 >= lo_max && c0 + 16 <= hi_min;
 #pragma unroll
           for (int j8 = 0; j8 < 2; ++j8) {
             uint32_t pw[4], dw[4];
@@ -468,7 +533,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
                   pv[e] = pr;
                   dv[e] = dr;
                 } else {
-                  const bool ok = lv && (uint32_t)(c0 + j - vlo) < (uint32_t)(vhi - vlo);
+                  const bool ok = (uint32_t)(c0 + j - vlo) < (uint32_t)(vhi - vlo);
                   pv[e] = ok ? pr : 0.f;
                   dv[e] = ok ? dr : 0.f;
                 }
@@ -614,20 +679,28 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
       ptx::mbar_wait(&sm.dq_full, tc & 1, status, 0x76000000u);
       ptx::tc_fence_after();
       {
+        // staging of dQ and dV: the K and dS buffers, or the in-block K / V
+        // buffers where there are some (their MMAs have completed too)
+        uint8_t* stage_q = sm.k;
+        uint8_t* stage_v = sm.ds;
+        if constexpr (kIn) {
+          stage_q = sm.kin;
+          stage_v = sm.vin;
+        }
         const bool complete = valid && blk_t < p.g.Gc;  // this lane's key is in a full block
         const int lb_t = valid ? blk_t - t.blk0 : 0;
         // b > 128: a sub-tile followed by others in its block adds their
         // contributions to its keys (and re-zeroes them)
         const bool cross = kSplit && valid && t.sub + 1 < block_tiles(p.g, t.blk0);
         const size_t xr = ((size_t)t.bh * p.G + t.blk0) * p.xrows + t.sub * kTileRows + row;
-        // dV (kv = 1: TMEM S columns -> dS buffer) or dK (kv = 0: dP columns ->
+        // dV (kv = 1: TMEM S columns -> dV staging) or dK (kv = 0: dP columns ->
         // P buffer) of the tile's keys, plus (summary gradient of the key's
         // block) / b and, for b > 128, the later sub-tiles' contributions
         auto stage_grad = [&](int kv) {
           const uint32_t tcol = kv ? kColSLast : kColDP;
           const float* srow = sm.sgrad[kv][lb_t];
           float* xrow = (kv ? p.dvx : p.dkx) + xr * D;
-          uint8_t* dst = kv ? sm.ds : sm.p;
+          uint8_t* dst = kv ? stage_v : sm.p;
 #pragma unroll 1
           for (int pc = 0; pc < kPartD / 16; ++pc) {
             const int col0 = part * kPartD + pc * 16;
@@ -670,8 +743,8 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
             for (int r = 0; r < t.rows; r += p.store_rows)
               ptx::tma_store_4d(tm, src + a * kAtomBytes + r * 128, a * 64, t.h, t.r0 + r, t.n);
         };
-        // 1. dQ (K buffer) and dV (dS buffer), stored as one bulk group: once it
-        // has been read, the next tile's first K and V chunks load there
+        // 1. dQ and dV, stored as one bulk group: once it has been read, the
+        // next tile's first K and V chunks (or its in-block K and V) load there
 #pragma unroll 1
         for (int pc = 0; pc < kPartD / 16; ++pc) {
           const int col0 = part * kPartD + pc * 16;
@@ -682,7 +755,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
 #pragma unroll
           for (int j8 = 0; j8 < 2; ++j8) {
             const uint32_t off = swz_offset(row, col0 + j8 * 8);
-            *reinterpret_cast<uint4*>(sm.k + off) = make_uint4(
+            *reinterpret_cast<uint4*>(stage_q + off) = make_uint4(
                 ptx::pack_bf16x2(__uint_as_float(gq[8 * j8]), __uint_as_float(gq[8 * j8 + 1])),
                 ptx::pack_bf16x2(__uint_as_float(gq[8 * j8 + 2]), __uint_as_float(gq[8 * j8 + 3])),
                 ptx::pack_bf16x2(__uint_as_float(gq[8 * j8 + 4]), __uint_as_float(gq[8 * j8 + 5])),
@@ -694,8 +767,8 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         ptx::fence_proxy_async_smem();
         ptx::named_barrier(1, kGradThreads);
         if (gtid == 0) {
-          issue_stores(&tm_dq, sm.k);
-          issue_stores(&tm_dv, sm.ds);
+          issue_stores(&tm_dq, stage_q);
+          issue_stores(&tm_dv, stage_v);
           ptx::tma_store_commit();
         }
         // 2. dK (P buffer), its own bulk group
@@ -711,8 +784,8 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         if (gtid == 0) {
           issue_stores(&tm_dk, sm.p);
           ptx::tma_store_commit();
-          // the dQ / dV group has been read: the K and dS buffers may take
-          // the next tile's first chunk loads (stage_free).  The P buffer is
+          // the dQ / dV group has been read: its buffers may take the next
+          // tile's loads (stage_free).  The P buffer is
           // rewritten only after the barrier that follows the next tile's
           // delta, before which this thread waits for the dK read.
           ptx::tma_store_wait_read_1();
@@ -839,7 +912,9 @@ int launch(const Problem& pr, const BwdTensorMaps& tm, const float* lse, TensorV
   p.ctrl = reinterpret_cast<uint32_t*>(ws + wl.ctrl);
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags_bwd);
   p.flags_stride = wl.tiles_per_seq;
-  const size_t smem = sizeof(BwdSmem<D>) + 1024;
+  const size_t smem = sizeof(BwdSmem<D, in_bufs<D, kSplit>()>) + 1024;
+  static_assert(sizeof(BwdSmem<D, in_bufs<D, kSplit>()>) + 1024 <= 227 * 1024,
+                "backward shared memory");
   auto kern = bwd_kernel<D, kSplit, kParts>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
