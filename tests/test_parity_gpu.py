@@ -116,6 +116,8 @@ def test_golden_fixture_fp32():
 @pytest.mark.parametrize("B,H,T,D,b", [
     (1, 2, 8192, 64, 96),    # partial last block (85 complete blocks + 32 rows)
     (2, 3, 200, 64, 16),     # ragged tail
+    (1, 2, 4000, 64, 64),    # two blocks per tile, partial last block
+    (1, 1, 4096, 64, 16),    # eight blocks per tile, two summary chunks
     (1, 2, 4096, 128, 64),
     (1, 2, 1000, 128, 128),  # T < ... with a partial block
     (1, 1, 100, 64, 128),    # a single partial block, no summaries at all
