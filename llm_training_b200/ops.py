@@ -10,6 +10,7 @@ autograd bookkeeping; all attention math runs in libsqrtblock.so.
 from __future__ import annotations
 
 import math
+import warnings
 import threading
 from typing import Optional
 
@@ -138,6 +139,21 @@ def _impl_code(impl: str) -> int:
         raise ValueError(f"impl must be one of {sorted(_lib.IMPLS)}, got {impl!r}") from None
 
 
+_simt_warned = False
+
+
+def _warn_simt_once():
+    """float32 inputs run on the CUDA-core kernels (the tensor-core kernels take
+    bfloat16): correct, but far slower.  Said once per process."""
+    global _simt_warned
+    if not _simt_warned:
+        _simt_warned = True
+        warnings.warn("sqrt_block_attention: float32 inputs run on the CUDA-core (SIMT) "
+                      "kernels, tens of times slower than the bfloat16 tensor-core kernels; "
+                      "cast q/k/v to bfloat16 or run under torch.autocast(dtype=torch.bfloat16)",
+                      RuntimeWarning, stacklevel=3)
+
+
 def sqrt_block_forward(q, k, v, block=None, scale=None, impl="auto"):
     """Forward only -> (o, lse, kbar, vbar).
 
@@ -159,6 +175,8 @@ def sqrt_block_forward(q, k, v, block=None, scale=None, impl="auto"):
     dev = q.device
     if _mailbox_words:
         check_status(dev)
+    if impl == "auto" and q.dtype == torch.float32:
+        _warn_simt_once()
     o = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
     lse = torch.empty((B, H, T), dtype=torch.float32, device=dev)
     kbar = torch.empty((B, H, Gc, D), dtype=q.dtype, device=dev)

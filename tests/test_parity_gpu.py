@@ -100,6 +100,18 @@ def test_cfg2_bf16_forward_backward(impl):
     check(q, k, v, do, 32, run(q, k, v, do, 32, impl), torch.bfloat16)
 
 
+def test_fp32_auto_warns_that_it_runs_on_cuda_cores():
+    """float32 under impl="auto" takes the SIMT kernels: said once, results unchanged."""
+    from llm_training_b200 import ops
+
+    ops._simt_warned = False
+    q, k, v, _ = inputs(1, 2, 256, 32, 3, torch.float32)
+    with pytest.warns(RuntimeWarning, match="CUDA-core"):
+        o1 = sqrt_block_forward(q, k, v)[0]
+    o2 = sqrt_block_forward(q, k, v, impl="simt")[0]
+    assert torch.equal(o1, o2)
+
+
 def test_golden_fixture_fp32():
     f = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden",
                                            "oracle_T200.npz"))
