@@ -700,7 +700,8 @@ def train_record(args, workload, world, rank, local, steps, warmup):
         exposed = max(ms - ms_ns, 0.0)
         rec["allreduce"] = {
             "collective": "DDP bucketed all-reduce of the fp32 gradients (NCCL, NVLink)",
-            "bucket_cap_mb": 25, "grad_bytes": nparam * 4,
+            "bucket_cap_mb": round(getattr(tr.model, "bucket_bytes_cap", 0) / 2**20, 1),
+            "grad_bytes": nparam * 4,
             "step_ms_without_allreduce": round(ms_ns, 3),
             "flat_allreduce_ms": round(ar_ms, 3),
             "flat_busbw_GBps": round(2 * (world - 1) / world * nparam * 4 / (ar_ms * 1e-3) / 1e9,
