@@ -19,10 +19,15 @@
 //   bwd: local_summary_p (P recomputed: the forward's workspace copy may have
 //        been overwritten by another layer of the same shape), dp_dglob,
 //        dglob_dsummary, local_grads (dQ, dK, dV)
+// For bf16 inputs with L in {16, 32, 64} and D in {64, 128} the local passes
+// (local_summary_p and local_grads) run on the tensor cores instead
+// (sqb_refsem_sm100.cu): 128-row tiles of whole blocks, bf16 operands, fp32
+// accumulation and fp32 softmax arithmetic.
 
 #include <math.h>
 
 #include "sqb_internal.cuh"
+#include "sqb_refsem_sm100.cuh"
 
 namespace sqb {
 namespace {
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(kThreads) local_grads_kernel(
 }
 
 struct RefsemWorkspace {
-  size_t P, dP, dglob, dsum, total;
+  size_t P, dP, dglob, dsum, status, total;
 };
 
 RefsemWorkspace refsem_layout(int64_t B, int64_t T, int64_t H, int64_t D) {
@@ -333,6 +338,8 @@ RefsemWorkspace refsem_layout(int64_t B, int64_t T, int64_t H, int64_t D) {
   off = align_up(off + (size_t)BH * L * L * 4, 256);
   w.dsum = off;
   off = align_up(off + (size_t)BH * L * L * 4, 256);
+  w.status = off;  // status words of the tensor-core kernel's waits
+  off = align_up(off + 64, 256);
   w.total = off;
   return w;
 }
@@ -363,16 +370,34 @@ bool set_smem(K kernel, size_t bytes) {
          cudaSuccess;
 }
 
+// The local maps, summaries (when requested) and P of every block: on the
+// tensor cores where refsem_tc_supported holds (bf16, L in {16, 32, 64}, D in
+// {64, 128}), else on CUDA cores.
+template <typename E>
+int local_pass(TensorView q, TensorView k, TensorView v, float* summary, float* P, uint8_t* ws,
+               const RefsemWorkspace& wl, int B, const RefsemParams& p, int dtype,
+               cudaStream_t s) {
+  if (refsem_tc_supported(p.L, p.D, dtype, {q, k, v})) {
+    uint32_t* status = reinterpret_cast<uint32_t*>(ws + wl.status);
+    if (cudaMemsetAsync(status, 0, 3 * sizeof(uint32_t), s) != cudaSuccess) return SQB_ERR_CUDA;
+    return refsem_tc_local(q, k, v, summary, P, B, p.G * p.L, p.H, p.D, p.L, p.scale, status,
+                           s);
+  }
+  const size_t sm1 = (size_t)(3 * p.L * tile_pitch(p.D) + p.L * p.L) * 4;
+  if (!set_smem(local_summary_p_kernel<E>, sm1)) return SQB_ERR_LAUNCH;
+  local_summary_p_kernel<E><<<dim3(p.G, B * p.H), kThreads, sm1, s>>>(q, k, v, summary, P, p);
+  return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
+}
+
 template <typename E>
 int refsem_forward(TensorView q, TensorView k, TensorView v, TensorView o, float* glob,
-                   float* summary, uint8_t* ws, const RefsemWorkspace& wl, int BH,
-                   const RefsemParams& p, cudaStream_t s) {
+                   float* summary, uint8_t* ws, const RefsemWorkspace& wl, int B,
+                   const RefsemParams& p, int dtype, cudaStream_t s) {
   float* P = reinterpret_cast<float*>(ws + wl.P);
-  const size_t sm1 = (size_t)(3 * p.L * tile_pitch(p.D) + p.L * p.L) * 4;
+  const int BH = B * p.H;
   const size_t sm2 = (size_t)(p.G * p.L + p.G * p.G) * 4;
-  if (!set_smem(local_summary_p_kernel<E>, sm1) || !set_smem(glob_kernel, sm2))
-    return SQB_ERR_LAUNCH;
-  local_summary_p_kernel<E><<<dim3(p.G, BH), kThreads, sm1, s>>>(q, k, v, summary, P, p);
+  if (!set_smem(glob_kernel, sm2)) return SQB_ERR_LAUNCH;
+  if (int e = local_pass<E>(q, k, v, summary, P, ws, wl, B, p, dtype, s)) return e;
   glob_kernel<<<BH, kThreads, sm2, s>>>(summary, glob, p);
   combine_kernel<E><<<dim3(p.G, BH), kThreads, 0, s>>>(P, glob, o, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
@@ -381,22 +406,29 @@ int refsem_forward(TensorView q, TensorView k, TensorView v, TensorView o, float
 template <typename E>
 int refsem_backward(TensorView q, TensorView k, TensorView v, TensorView dout, const float* glob,
                     const float* summary, TensorView dq, TensorView dk, TensorView dv,
-                    uint8_t* ws, const RefsemWorkspace& wl, int BH, const RefsemParams& p,
-                    cudaStream_t s) {
+                    uint8_t* ws, const RefsemWorkspace& wl, int B, const RefsemParams& p,
+                    int dtype, cudaStream_t s) {
+  const int BH = B * p.H;
   float* P = reinterpret_cast<float*>(ws + wl.P);
   float* dP = reinterpret_cast<float*>(ws + wl.dP);
   float* dglob = reinterpret_cast<float*>(ws + wl.dglob);
   float* dsum = reinterpret_cast<float*>(ws + wl.dsum);
-  const size_t sm1 = (size_t)(3 * p.L * tile_pitch(p.D) + p.L * p.L) * 4;
   const size_t sm2 = (size_t)(p.L * p.D) * 4;
   const size_t sm3 = (size_t)(p.G * p.G + p.G * p.L) * 4;
   const size_t sm4 = (size_t)(4 * p.L * tile_pitch(p.D) + 2 * p.L * p.L) * 4;
-  if (!set_smem(local_summary_p_kernel<E>, sm1) || !set_smem(dp_dglob_kernel<E>, sm2) ||
-      !set_smem(dglob_dsummary_kernel, sm3) || !set_smem(local_grads_kernel<E>, sm4))
+  if (!set_smem(dp_dglob_kernel<E>, sm2) || !set_smem(dglob_dsummary_kernel, sm3) ||
+      !set_smem(local_grads_kernel<E>, sm4))
     return SQB_ERR_LAUNCH;
-  local_summary_p_kernel<E><<<dim3(p.G, BH), kThreads, sm1, s>>>(q, k, v, nullptr, P, p);
+  if (int e = local_pass<E>(q, k, v, nullptr, P, ws, wl, B, p, dtype, s)) return e;
   dp_dglob_kernel<E><<<dim3(p.G, BH), kThreads, sm2, s>>>(dout, P, glob, dP, dglob, p);
   dglob_dsummary_kernel<<<BH, kThreads, sm3, s>>>(glob, dglob, summary, dsum, p);
+  if (refsem_tc_supported(p.L, p.D, dtype, {q, k, v, dq, dk, dv})) {
+    uint32_t* status = reinterpret_cast<uint32_t*>(ws + wl.status);
+    if (int e = refsem_tc_grads(q, k, v, dP, dsum, dq, dk, dv, B, p.G * p.L, p.H, p.D, p.L,
+                                p.scale, status, s))
+      return e;
+    return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
+  }
   local_grads_kernel<E><<<dim3(p.G, BH), kThreads, sm4, s>>>(q, k, v, dP, dsum, dq, dk, dv, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
@@ -434,9 +466,9 @@ int sqb_refsem_fwd(const void* q, const void* k, const void* v, void* o, float* 
   cudaGetLastError();
   if (dtype == SQB_F32)
     return refsem_forward<float>(tq, tk, tv, to, glob, summary, (uint8_t*)workspace, wl,
-                                 (int)(B * H), p, s);
+                                 (int)B, p, dtype, s);
   return refsem_forward<__nv_bfloat16>(tq, tk, tv, to, glob, summary, (uint8_t*)workspace, wl,
-                                       (int)(B * H), p, s);
+                                       (int)B, p, dtype, s);
 }
 
 int sqb_refsem_bwd(const void* q, const void* k, const void* v, const void* dout,
@@ -462,9 +494,9 @@ int sqb_refsem_bwd(const void* q, const void* k, const void* v, const void* dout
   cudaGetLastError();
   if (dtype == SQB_F32)
     return refsem_backward<float>(tq, tk, tv, tdo, glob, summary, tdq, tdk, tdv,
-                                  (uint8_t*)workspace, wl, (int)(B * H), p, s);
+                                  (uint8_t*)workspace, wl, (int)B, p, dtype, s);
   return refsem_backward<__nv_bfloat16>(tq, tk, tv, tdo, glob, summary, tdq, tdk, tdv,
-                                        (uint8_t*)workspace, wl, (int)(B * H), p, s);
+                                        (uint8_t*)workspace, wl, (int)B, p, dtype, s);
 }
 
 }  // extern "C"

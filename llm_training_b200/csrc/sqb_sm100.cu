@@ -101,6 +101,24 @@ bool encode_summaries(CUtensorMap* m, const Problem& p, const void* ptr) {
 
 }  // namespace
 
+bool sm100_device(int* num_sms) { return encode_fn() != nullptr && device_ok(num_sms); }
+
+bool sm100_views_ok(std::initializer_list<TensorView> views) {
+  for (const TensorView& t : views)
+    if (!view_ok(t)) return false;
+  return true;
+}
+
+bool sm100_encode_rows(CUtensorMap* m, int B, int T, int H, int D, const TensorView& t,
+                       int rows) {
+  Problem p{};
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.D = D;
+  return encode_bthd(m, p, t, rows);
+}
+
 bool sm100_fwd_supported(const Problem& p, std::initializer_list<TensorView> views,
                          const float* lse, const void* kbar, const void* vbar) {
   return common_ok(p, views, lse, kbar, vbar);

@@ -18,6 +18,15 @@ bool sm100_fwd_supported(const Problem& p, std::initializer_list<TensorView> vie
 bool sm100_bwd_supported(const Problem& p, std::initializer_list<TensorView> views,
                          const float* lse, const void* kbar, const void* vbar);
 
+// Shared with the reference-semantics tensor-core kernels: an sm_100-class
+// device (and its SM count), bf16 views the TMA maps accept (16-byte aligned,
+// strides multiples of 8 elements), and a (B, T, H, D) bf16 view as a load map
+// with box {64 columns, 1 head, rows, 1 batch} and the 128-byte swizzle.
+bool sm100_device(int* num_sms);
+bool sm100_views_ok(std::initializer_list<TensorView> views);
+bool sm100_encode_rows(CUtensorMap* m, int B, int T, int H, int D, const TensorView& t,
+                       int rows);
+
 int sm100_forward(const Problem& p, TensorView q, TensorView k, TensorView v, TensorView o,
                   float* lse, void* kbar, void* vbar, uint8_t* ws, const WorkspaceLayout& wl,
                   cudaStream_t stream);

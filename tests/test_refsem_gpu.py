@@ -54,7 +54,7 @@ def test_fp32_matches_reference_fixture(T):
 
 
 @pytest.mark.parametrize("B,H,T,D", [(2, 4, 256, 32), (8, 12, 1024, 64), (1, 2, 4096, 128),
-                                     (1, 3, 64, 16), (2, 1, 1, 8)])
+                                     (2, 4, 256, 64), (1, 3, 64, 16), (2, 1, 1, 8)])
 def test_bf16_matches_oracle(B, H, T, D):
     g = torch.Generator().manual_seed(T + D)
     q, k, v, do = (torch.randn(B, T, H, D, generator=g).to(torch.bfloat16).cuda() for _ in range(4))
