@@ -15,10 +15,12 @@
 // fp32 and bf16 inputs; L <= 64 and D <= 128 (the reference runs L = 16..32).
 //
 // Kernels, one CTA of 256 threads per (block i, batch*head) or per batch*head:
-//   fwd: local_summary_p (local map, summary, P), glob_softmax, combine
+//   fwd: local_summary_p (local map, summary, P), glob_softmax, combine (one
+//        CTA per row l of every block: each P row read once)
 //   bwd: local_summary_p (P recomputed: the forward's workspace copy may have
-//        been overwritten by another layer of the same shape), dp_dglob,
-//        dglob_dsummary, local_grads (dQ, dK, dV)
+//        been overwritten by another layer of the same shape), dp_dglob (per
+//        row l like the combine; d_glob as L row shares), dglob_dsummary,
+//        local_grads (dQ, dK, dV)
 // For bf16 inputs with L in {16, 32, 64} and D in {64, 128} the local passes
 // (local_summary_p and local_grads) run on the tensor cores instead
 // (sqb_refsem_sm100.cu): 128-row tiles of whole blocks, bf16 operands, fp32
@@ -183,69 +185,97 @@ __global__ void __launch_bounds__(kThreads) glob_kernel(const float* summary, fl
   }
 }
 
-// Per (block i, bh): out_i = P_i + sum_{j<i} glob[i, j] P_j.
+// Per (row l of every block, bh): out_i[l] = P_i[l] + sum_{j<i} glob[i, j] P_j[l]
+// for every block i.  Each P row is read once; the glob matrix and the G rows
+// l of P sit in shared memory.
 template <typename E>
 __global__ void __launch_bounds__(kThreads) combine_kernel(const float* P, const float* glob,
                                                            TensorView o, RefsemParams p) {
-  const int i = blockIdx.x, bh = blockIdx.y, n = bh / p.H, h = bh % p.H;
-  const int L = p.L, D = p.D;
-  const float* gi = glob + ((size_t)bh * p.G + i) * p.G;
-  const float* Pb = P + (size_t)bh * p.G * L * D;
-  for (int e = threadIdx.x; e < L * D; e += kThreads) {
-    float acc = Pb[(size_t)i * L * D + e];
-    for (int j = 0; j < i; ++j) acc += gi[j] * Pb[(size_t)j * L * D + e];
-    const int l = e / D, d = e % D;
+  extern __shared__ float sm[];
+  const int l = blockIdx.x, bh = blockIdx.y, n = bh / p.H, h = bh % p.H;
+  const int L = p.L, D = p.D, G = p.G;
+  float* sg = sm;           // G x G
+  float* sp = sg + G * G;   // G x D: row l of every block
+  const float* gb = glob + (size_t)bh * G * G;
+  for (int e = threadIdx.x; e < G * G; e += kThreads) sg[e] = gb[e];
+  for (int e = threadIdx.x; e < G * D; e += kThreads) {
+    const int i = e / D, d = e % D;
+    sp[e] = P[(((size_t)bh * G + i) * L + l) * D + d];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += kThreads) {
+    const int i = e / D, d = e % D;
+    float acc = sp[e];
+    for (int j = 0; j < i; ++j) acc += sg[i * G + j] * sp[j * D + d];
     st_f(at_w<E>(o, n, i * L + l, h) + d, acc);
   }
 }
 
-// Per (block j, bh): dP_j = dO_j + sum_{i>j} glob[i, j] dO_i, and row j of
-// d_glob: d_glob[j, c] = <dO_j, P_c> for c < j.
+// Per (row l of every block, bh): dP_j[l] = dO_j[l] + sum_{i>j} glob[i, j] dO_i[l]
+// for every block j, and this row's share of d_glob:
+// part[l][j, c] = <dO_j[l], P_c[l]> for c < j (zero otherwise).  d_glob is the
+// sum of the L shares, added in a fixed order by dglob_dsummary_kernel.
 template <typename E>
 __global__ void __launch_bounds__(kThreads) dp_dglob_kernel(TensorView dout, const float* P,
                                                             const float* glob, float* dP,
-                                                            float* dglob, RefsemParams p) {
+                                                            float* dglob_part, RefsemParams p) {
   extern __shared__ float sm[];
-  const int j = blockIdx.x, bh = blockIdx.y, n = bh / p.H, h = bh % p.H;
-  const int L = p.L, D = p.D, G = p.G;
-  float* sdo = sm;  // dO_j, L x D, contiguous (read along rows only)
-  load_tile<E>(sdo, dout, n, h, j, p, D);
-  __syncthreads();
+  const int l = blockIdx.x, bh = blockIdx.y, n = bh / p.H, h = bh % p.H;
+  const int L = p.L, D = p.D, G = p.G, ld = D + 1;
+  float* sg = sm;            // G x G
+  float* sdo = sg + G * G;   // G x ld: row l of every block's dO (padded pitch)
+  float* sp = sdo + G * ld;  // G x ld: row l of every block's P
   const float* gb = glob + (size_t)bh * G * G;
-  float* dPj = dP + ((size_t)bh * G + j) * L * D;
-  for (int e = threadIdx.x; e < L * D; e += kThreads) {
-    const int l = e / D, d = e % D;
-    float acc = sdo[e];
-    for (int i = j + 1; i < G; ++i) acc += gb[(size_t)i * G + j] * ld_f(at<E>(dout, n, i * L + l, h) + d);
-    dPj[e] = acc;
+  for (int e = threadIdx.x; e < G * G; e += kThreads) sg[e] = gb[e];
+  for (int e = threadIdx.x; e < G * D; e += kThreads) {
+    const int i = e / D, d = e % D;
+    sdo[i * ld + d] = ld_f(at<E>(dout, n, i * L + l, h) + d);
+    sp[i * ld + d] = P[(((size_t)bh * G + i) * L + l) * D + d];
   }
-  const float* Pb = P + (size_t)bh * G * L * D;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* dg = dglob + ((size_t)bh * G + j) * G;
-  // one warp per earlier block c: d_glob[j, c] = <dO_j, P_c>, zero for c >= j
-  for (int c = warp; c < j; c += kThreads / 32) {
-    const float* Pc = Pb + (size_t)c * L * D;
-    float part = 0.f;
-    for (int e = lane; e < L * D; e += 32) part += sdo[e] * Pc[e];
-    part = warp_sum(part);
-    if (lane == 0) dg[c] = part;
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += kThreads) {
+    const int j = e / D, d = e % D;
+    float acc = sdo[j * ld + d];
+    for (int i = j + 1; i < G; ++i) acc += sg[i * G + j] * sdo[i * ld + d];
+    dP[(((size_t)bh * G + j) * L + l) * D + d] = acc;
   }
-  for (int c = j + threadIdx.x; c < G; c += kThreads) dg[c] = 0.f;
+  float* part = dglob_part + ((size_t)bh * L + l) * G * G;
+  for (int e = threadIdx.x; e < G * G; e += kThreads) {
+    const int j = e / G, c = e % G;
+    float acc = 0.f;
+    if (c < j)
+      for (int d = 0; d < D; ++d) acc += sdo[j * ld + d] * sp[c * ld + d];
+    part[e] = acc;
+  }
 }
 
-// Per bh: d_gs = glob * (d_glob - rowsum(glob * d_glob)); d_summary =
-// (d_gs + d_gs^T) summary / sqrt(L).
+// Per bh: d_glob = the sum of the L row shares (in row order); d_gs = glob *
+// (d_glob - rowsum(glob * d_glob)); d_summary = (d_gs + d_gs^T) summary / sqrt(L).
 __global__ void __launch_bounds__(kThreads) dglob_dsummary_kernel(const float* glob,
-                                                                  const float* dglob,
+                                                                  const float* dglob_part,
                                                                   const float* summary,
                                                                   float* dsum, RefsemParams p) {
   extern __shared__ float sm[];
   const int bh = blockIdx.x, G = p.G, L = p.L;
   float* dgs = sm;          // G x G
   float* s = dgs + G * G;   // G x L
+  float* db = s + G * L;    // G x G: d_glob
   const float* gb = glob + (size_t)bh * G * G;
-  const float* db = dglob + (size_t)bh * G * G;
+  const float* pb = dglob_part + (size_t)bh * L * G * G;
+  for (int e = threadIdx.x; e < G * G; e += kThreads) {
+    // eight independent partial sums (rows l = u mod 8), combined in a fixed
+    // order: the loads of one element overlap instead of forming one chain
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int l = 0;
+    for (; l + 8 <= L; l += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] += pb[(size_t)(l + u) * G * G + e];
+    }
+    for (; l < L; ++l) a[0] += pb[(size_t)l * G * G + e];
+    db[e] = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+  }
   for (int e = threadIdx.x; e < G * L; e += kThreads) s[e] = summary[(size_t)bh * G * L + e];
+  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int a = warp; a < G; a += kThreads / 32) {
     float r = 0.f;
@@ -322,7 +352,7 @@ __global__ void __launch_bounds__(kThreads) local_grads_kernel(
 }
 
 struct RefsemWorkspace {
-  size_t P, dP, dglob, dsum, status, total;
+  size_t P, dP, dglob_part, dsum, status, total;
 };
 
 RefsemWorkspace refsem_layout(int64_t B, int64_t T, int64_t H, int64_t D) {
@@ -334,8 +364,8 @@ RefsemWorkspace refsem_layout(int64_t B, int64_t T, int64_t H, int64_t D) {
   off = align_up(off + (size_t)BH * T * D * 4, 256);
   w.dP = off;
   off = align_up(off + (size_t)BH * T * D * 4, 256);
-  w.dglob = off;
-  off = align_up(off + (size_t)BH * L * L * 4, 256);
+  w.dglob_part = off;  // (B*H, L, G, G) row shares of d_glob (G = L)
+  off = align_up(off + (size_t)BH * L * L * L * 4, 256);
   w.dsum = off;
   off = align_up(off + (size_t)BH * L * L * 4, 256);
   w.status = off;  // status words of the tensor-core kernel's waits
@@ -397,9 +427,11 @@ int refsem_forward(TensorView q, TensorView k, TensorView v, TensorView o, float
   const int BH = B * p.H;
   const size_t sm2 = (size_t)(p.G * p.L + p.G * p.G) * 4;
   if (!set_smem(glob_kernel, sm2)) return SQB_ERR_LAUNCH;
+  const size_t sm3 = (size_t)(p.G * p.G + p.G * p.D) * 4;
+  if (!set_smem(combine_kernel<E>, sm3)) return SQB_ERR_LAUNCH;
   if (int e = local_pass<E>(q, k, v, summary, P, ws, wl, B, p, dtype, s)) return e;
   glob_kernel<<<BH, kThreads, sm2, s>>>(summary, glob, p);
-  combine_kernel<E><<<dim3(p.G, BH), kThreads, 0, s>>>(P, glob, o, p);
+  combine_kernel<E><<<dim3(p.L, BH), kThreads, sm3, s>>>(P, glob, o, p);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 
@@ -411,17 +443,17 @@ int refsem_backward(TensorView q, TensorView k, TensorView v, TensorView dout, c
   const int BH = B * p.H;
   float* P = reinterpret_cast<float*>(ws + wl.P);
   float* dP = reinterpret_cast<float*>(ws + wl.dP);
-  float* dglob = reinterpret_cast<float*>(ws + wl.dglob);
+  float* dglob_part = reinterpret_cast<float*>(ws + wl.dglob_part);
   float* dsum = reinterpret_cast<float*>(ws + wl.dsum);
-  const size_t sm2 = (size_t)(p.L * p.D) * 4;
-  const size_t sm3 = (size_t)(p.G * p.G + p.G * p.L) * 4;
+  const size_t sm2 = (size_t)(p.G * p.G + 2 * p.G * (p.D + 1)) * 4;
+  const size_t sm3 = (size_t)(2 * p.G * p.G + p.G * p.L) * 4;
   const size_t sm4 = (size_t)(4 * p.L * tile_pitch(p.D) + 2 * p.L * p.L) * 4;
   if (!set_smem(dp_dglob_kernel<E>, sm2) || !set_smem(dglob_dsummary_kernel, sm3) ||
       !set_smem(local_grads_kernel<E>, sm4))
     return SQB_ERR_LAUNCH;
   if (int e = local_pass<E>(q, k, v, nullptr, P, ws, wl, B, p, dtype, s)) return e;
-  dp_dglob_kernel<E><<<dim3(p.G, BH), kThreads, sm2, s>>>(dout, P, glob, dP, dglob, p);
-  dglob_dsummary_kernel<<<BH, kThreads, sm3, s>>>(glob, dglob, summary, dsum, p);
+  dp_dglob_kernel<E><<<dim3(p.L, BH), kThreads, sm2, s>>>(dout, P, glob, dP, dglob_part, p);
+  dglob_dsummary_kernel<<<BH, kThreads, sm3, s>>>(glob, dglob_part, summary, dsum, p);
   if (refsem_tc_supported(p.L, p.D, dtype, {q, k, v, dq, dk, dv})) {
     uint32_t* status = reinterpret_cast<uint32_t*>(ws + wl.status);
     if (int e = refsem_tc_grads(q, k, v, dP, dsum, dq, dk, dv, B, p.G * p.L, p.H, p.D, p.L,
