@@ -103,6 +103,9 @@ struct BwdSmem : BwdInBufs<D, kIn> {
   uint64_t ld_full, ld_empty, k_full, k_empty, v_full, v_empty, s_full, ps_full, g_full, g_free;
   uint64_t delta_done, stage_free;
   uint64_t red_done, pub_read, sums_ready, sgrad_free;
+  // the dV half (columns 0-127) of a drained chunk has been read: the tile's
+  // last chunk may compute its dP there while the dK half is still drained
+  uint64_t lo_free;
   uint64_t mma_done;  // exit: every MMA of the CTA has completed
   uint64_t dq_full;   // the tile's dQ accumulation is complete
   uint64_t in_full;   // the in-block K / V buffers have landed (in_bufs)
@@ -120,8 +123,18 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // TMEM columns: S / dV chunk at 0, dP / dK chunk at 128, dQ at 256; the
 // tile's last chunk takes S / dV at 384, so its S is computed while the
-// previous chunk's gradients are still read out of columns 0-255.
+// previous chunk's gradients are still read out of columns 0-255.  For b > 128
+// (several drained chunks per tile) the last chunk also takes dP / dK at 0,
+// so its dP is computed as soon as the previous chunk's dV half (0-127) has
+// been read, while the dK half (128-255) is still being drained (the drains
+// then read the two halves in two passes).  Measured: T=32K 1.140 -> 1.084 ms
+// backward; with b <= 128 the two-pass drain cost more than it gained
+// (T=16K +1.9 %, T=8K +2.1 %).
 constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256, kColSLast = 384;
+template <bool kSplit>
+constexpr uint32_t col_dp_last() {
+  return kSplit ? 0u : kColDP;
+}
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
@@ -168,6 +181,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
     ptx::mbar_init(&sm.ps_full, kGradWarps);
     ptx::mbar_init(&sm.g_full, 1);
     ptx::mbar_init(&sm.g_free, kGradWarps);
+    ptx::mbar_init(&sm.lo_free, kGradWarps);  // one arrive per gradient warp
     ptx::mbar_init(&sm.mma_done, 1);
     ptx::mbar_init(&sm.dq_full, 1);
     ptx::mbar_init(&sm.in_full, 1);
@@ -342,6 +356,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         vin_s = ptx::smem_u32(sm.vin);
       }
       int tc = 0, kc = 0, kv = 0;  // kv: chunks read from the K / V buffers
+      int lc = 0;                  // drained (non-last) chunks: lo_free phases
       while (true) {
         ptx::mbar_wait(&sm.ld_full, tc & 1, status, 0x60000000u);
         const int n = sm.tile_ring;
@@ -351,10 +366,13 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         const int nch = t.nsc + t.nin;
         for (int c = 0; c < nch; ++c) {
           const int N = c < t.nsc ? sum_chunk(t, c).n16 : in_chunk<kSplit>(t, c - t.nsc).n;
-          // a later last chunk's S goes to free columns: only its dP waits for
-          // the previous chunk's gradients to be read (g_free)
-          const bool late_last = c > 0 && c == nch - 1;
-          const uint32_t col_s = c == nch - 1 ? kColSLast : kColS;
+          // a later last chunk's S goes to free columns, and its dP only waits
+          // for the dV half of the previous chunk's gradients to be read
+          // (lo_free), not for the whole drain (g_free)
+          const bool last = c == nch - 1;
+          const bool late_last = c > 0 && last;
+          const uint32_t col_s = last ? kColSLast : kColS;
+          const uint32_t col_dp = last ? col_dp_last<kSplit>() : kColDP;
           const bool inb = kIn && c == t.nsc;  // K / V in the in-block buffers
           const uint32_t kc_s = inb ? kin_s : k_s;
           if (inb)
@@ -370,13 +388,18 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
             ptx::mma_ss(tmem + col_s, desc_kmajor(q_s, kk), desc_kmajor(kc_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
           if (!inb) ptx::mbar_wait(&sm.v_full, kv & 1, status, 0x64000000u);
-          if (late_last) ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
+          if (late_last) {
+            if constexpr (kSplit)
+              ptx::mbar_wait(&sm.lo_free, (lc - 1) & 1, status, 0x66000000u);
+            else
+              ptx::mbar_wait(&sm.g_free, (kc - 1) & 1, status, 0x62000000u);
+          }
           ptx::tc_fence_after();
           // where this chunk's V is
           const uint32_t vc_s = inb ? vin_s : (c == 0 && t.nsc > 0) ? ds_s : v_s;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            ptx::mma_ss(tmem + kColDP, desc_kmajor(do_s, kk), desc_kmajor(vc_s, kk), idesc_s,
+            ptx::mma_ss(tmem + col_dp, desc_kmajor(do_s, kk), desc_kmajor(vc_s, kk), idesc_s,
                         kk > 0 ? 1u : 0u);
           ptx::mma_commit(&sm.s_full);
           if (!inb) ptx::mma_commit(&sm.v_empty);  // the V chunk is read only by dP
@@ -399,7 +422,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
               ptx::mma_ss(tmem + col_s, desc_mnmajor(p_s, kk), desc_mnmajor(do_s, kk), idesc_dvdk,
                           kk > 0 ? 1u : 0u);
             for (int kk = 0; kk < kq; ++kk)  // dKc = dS^T Q
-              ptx::mma_ss(tmem + kColDP, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
+              ptx::mma_ss(tmem + col_dp, desc_mnmajor(ds_s, kk), desc_mnmajor(q_s, kk), idesc_dvdk,
                           kk > 0 ? 1u : 0u);
           }
           ptx::mma_commit(&sm.g_full);
@@ -411,6 +434,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
           if (c == nch - 1) ptx::mma_commit(&sm.dq_full);
           ++kc;
           if (!inb) ++kv;
+          if (!last) ++lc;
         }
         ++tc;
       }
@@ -476,7 +500,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
       for (int i = 1; i < kParts; ++i) delta += sm.dpart[i][row];
 
       // P and dS of one chunk into smem (this part's key columns; masked -> 0)
-      auto softmax_grad = [&](int N, int vlo, int vhi, uint32_t col_s) {
+      auto softmax_grad = [&](int N, int vlo, int vhi, uint32_t col_s, uint32_t col_dp) {
         const bool any_col = vhi > vlo;
         const int wlo = __reduce_min_sync(0xffffffffu, any_col ? vlo : 0x7fffffff);
         const int whi = __reduce_max_sync(0xffffffffu, any_col ? vhi : 0);
@@ -498,7 +522,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         auto load = [&](int pi, uint32_t (&sv)[16], uint32_t (&dp)[16]) {
           if (live(pi)) {
             ptx::tmem_ld16(tmem + lane_off + col_s + col0(pi), sv);
-            ptx::tmem_ld16(tmem + lane_off + kColDP + col0(pi), dp);
+            ptx::tmem_ld16(tmem + lane_off + col_dp + col0(pi), dp);
           }
         };
         // P = exp2(S*c - L), dS = P * (dP*scale - delta*scale); masked -> 0.
@@ -570,39 +594,66 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
       // atomics, then frees the columns for the next chunk's S/dP.
       // store: plain stores instead of atomic additions (a destination with a
       // single writer)
+      // b > 128: two passes, dV (columns 0-127), after which lo_free lets the
+      // tile's last chunk compute its dP there, then dK (columns 128-255),
+      // g_free; otherwise both halves of a piece at once, then g_free.
       auto drain = [&](float* dkrow, float* dvrow, bool ok, bool store) {
+        if constexpr (!kSplit) {
 #pragma unroll 1
-        for (int pc = 0; pc < kPartD / 16; ++pc) {
-          const int col0 = part * kPartD + pc * 16;
-          uint32_t gv[16], gk[16];
-          ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
-          ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
-          ptx::tmem_wait_ld();
-          ptx::reg_fence(gv);
-          ptx::reg_fence(gk);
-          if (ok && store) {
+          for (int pc = 0; pc < kPartD / 16; ++pc) {
+            const int col0 = part * kPartD + pc * 16;
+            uint32_t gv[16], gk[16];
+            ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
+            ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(gv);
+            ptx::reg_fence(gk);
+            if (ok) {
 #pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-              __stcg(reinterpret_cast<uint4*>(dvrow + col0 + 4 * j4),
-                     make_uint4(gv[4 * j4], gv[4 * j4 + 1], gv[4 * j4 + 2], gv[4 * j4 + 3]));
-              __stcg(reinterpret_cast<uint4*>(dkrow + col0 + 4 * j4),
-                     make_uint4(gk[4 * j4], gk[4 * j4 + 1], gk[4 * j4 + 2], gk[4 * j4 + 3]));
-            }
-          } else if (ok) {
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-              ptx::red_add_v4(dvrow + col0 + 4 * j4, __uint_as_float(gv[4 * j4]),
-                              __uint_as_float(gv[4 * j4 + 1]), __uint_as_float(gv[4 * j4 + 2]),
-                              __uint_as_float(gv[4 * j4 + 3]));
-              ptx::red_add_v4(dkrow + col0 + 4 * j4, __uint_as_float(gk[4 * j4]),
-                              __uint_as_float(gk[4 * j4 + 1]), __uint_as_float(gk[4 * j4 + 2]),
-                              __uint_as_float(gk[4 * j4 + 3]));
+              for (int j4 = 0; j4 < 4; ++j4) {
+                ptx::red_add_v4(dvrow + col0 + 4 * j4, __uint_as_float(gv[4 * j4]),
+                                __uint_as_float(gv[4 * j4 + 1]), __uint_as_float(gv[4 * j4 + 2]),
+                                __uint_as_float(gv[4 * j4 + 3]));
+                ptx::red_add_v4(dkrow + col0 + 4 * j4, __uint_as_float(gk[4 * j4]),
+                                __uint_as_float(gk[4 * j4 + 1]), __uint_as_float(gk[4 * j4 + 2]),
+                                __uint_as_float(gk[4 * j4 + 3]));
+              }
             }
           }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+          ++kc;
+          return;
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t tcol = half == 0 ? kColS : kColDP;
+          float* dst = half == 0 ? dvrow : dkrow;
+#pragma unroll 1
+          for (int pc = 0; pc < kPartD / 16; ++pc) {
+            const int col0 = part * kPartD + pc * 16;
+            uint32_t g[16];
+            ptx::tmem_ld16(tmem + lane_off + tcol + col0, g);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(g);
+            if (ok && store) {
+#pragma unroll
+              for (int j4 = 0; j4 < 4; ++j4)
+                __stcg(reinterpret_cast<uint4*>(dst + col0 + 4 * j4),
+                       make_uint4(g[4 * j4], g[4 * j4 + 1], g[4 * j4 + 2], g[4 * j4 + 3]));
+            } else if (ok) {
+#pragma unroll
+              for (int j4 = 0; j4 < 4; ++j4)
+                ptx::red_add_v4(dst + col0 + 4 * j4, __uint_as_float(g[4 * j4]),
+                                __uint_as_float(g[4 * j4 + 1]), __uint_as_float(g[4 * j4 + 2]),
+                                __uint_as_float(g[4 * j4 + 3]));
+            }
+          }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(half == 0 ? &sm.lo_free : &sm.g_free);
+        }
         ++kc;
       };
 
@@ -613,36 +664,64 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         const int clo = sc.lo - sc.w, chi = sc.e - sc.w;  // columns of real summaries
         float* dvb = p.dvbar + (size_t)t.bh * p.g.Gc * D + row;
         float* dkb = p.dkbar + (size_t)t.bh * p.g.Gc * D + row;
+        if constexpr (!kSplit) {
 #pragma unroll 1
-        for (int pc = 0; pc < kPieces; ++pc) {
-          const int col0 = (pc * kParts + part) * 16;  // interleaved as in softmax_grad
-          if (col0 + 16 <= clo || col0 >= chi) continue;  // warp-uniform
-          uint32_t gv[16], gk[16];
-          ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
-          ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
-          ptx::tmem_wait_ld();
-          ptx::reg_fence(gv);
-          ptx::reg_fence(gk);
+          for (int pc = 0; pc < kPieces; ++pc) {
+            const int col0 = (pc * kParts + part) * 16;  // interleaved as in softmax_grad
+            if (col0 + 16 <= clo || col0 >= chi) continue;  // warp-uniform
+            uint32_t gv[16], gk[16];
+            ptx::tmem_ld16(tmem + lane_off + kColS + col0, gv);
+            ptx::tmem_ld16(tmem + lane_off + kColDP + col0, gk);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(gv);
+            ptx::reg_fence(gk);
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int col = col0 + jj;
-            if (col >= clo && col < chi) {
-              const size_t off = (size_t)(sc.w + col) * D;
-              ptx::red_add_f32(dvb + off, __uint_as_float(gv[jj]));
-              ptx::red_add_f32(dkb + off, __uint_as_float(gk[jj]));
+            for (int jj = 0; jj < 16; ++jj) {
+              const int col = col0 + jj;
+              if (col >= clo && col < chi) {
+                const size_t off = (size_t)(sc.w + col) * D;
+                ptx::red_add_f32(dvb + off, __uint_as_float(gv[jj]));
+                ptx::red_add_f32(dkb + off, __uint_as_float(gk[jj]));
+              }
             }
           }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+          ++kc;
+          return;
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&sm.g_free);
+        // b > 128: two passes as in drain, dVbar^T (then lo_free), dKbar^T
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t tcol = half == 0 ? kColS : kColDP;
+          float* dst = half == 0 ? dvb : dkb;
+#pragma unroll 1
+          for (int pc = 0; pc < kPieces; ++pc) {
+            const int col0 = (pc * kParts + part) * 16;  // interleaved as in softmax_grad
+            if (col0 + 16 <= clo || col0 >= chi) continue;  // warp-uniform
+            uint32_t g[16];
+            ptx::tmem_ld16(tmem + lane_off + tcol + col0, g);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(g);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int col = col0 + jj;
+              if (col >= clo && col < chi)
+                ptx::red_add_f32(dst + (size_t)(sc.w + col) * D, __uint_as_float(g[jj]));
+            }
+          }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(half == 0 ? &sm.lo_free : &sm.g_free);
+        }
         ++kc;
       };
 
       // ---- summary chunks: add dKc / dVc to the summary accumulators
       for (int c = 0; c < t.nsc; ++c) {
         const SumChunk sc = sum_chunk(t, c);
-        softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w, kColS);
+        softmax_grad(sc.n16, sc.lo - sc.w, min(sc.e, lim) - sc.w, kColS, kColDP);
         if constexpr (kTransposedSums) {
           drain_sums_t(sc);
         } else {
@@ -658,7 +737,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
       // sub-tiles of the block and are added to the workspace accumulators
       // that those sub-tiles' epilogues read.
       for (int u = 0; u + 1 < t.nin; ++u) {
-        softmax_grad(kTileRows, 0, valid ? kTileRows : 0, kColS);
+        softmax_grad(kTileRows, 0, valid ? kTileRows : 0, kColS, kColDP);
         const size_t xr = ((size_t)t.bh * p.G + t.blk0) * p.xrows + u * kTileRows + row;
         // with two sub-tiles per block (b <= 256) a key's cross contribution
         // has one writer: stored, and never re-zeroed (each launch rewrites it
@@ -672,7 +751,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
 
       // ---- the in-block chunk of the tile's own rows (causal)
       softmax_grad(t.n_in, valid ? max(0, blk_t * p.g.b - t.r0) : 0, valid ? row + 1 : 0,
-                   kColSLast);
+                   kColSLast, col_dp_last<kSplit>());
       // the publisher has staged sum / b of the tile's complete blocks
       ptx::mbar_wait(&sm.sums_ready, tc & 1, status, 0x73000000u);
       // dQ (the tile's last MMA) has read dS: the dS buffer may take dV staging
@@ -697,7 +776,7 @@ __global__ void __launch_bounds__(bwd_threads<kParts>(), 1)
         // P buffer) of the tile's keys, plus (summary gradient of the key's
         // block) / b and, for b > 128, the later sub-tiles' contributions
         auto stage_grad = [&](int kv) {
-          const uint32_t tcol = kv ? kColSLast : kColDP;
+          const uint32_t tcol = kv ? kColSLast : col_dp_last<kSplit>();
           const float* srow = sm.sgrad[kv][lb_t];
           float* xrow = (kv ? p.dvx : p.dkx) + xr * D;
           uint8_t* dst = kv ? stage_v : sm.p;
