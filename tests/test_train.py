@@ -69,6 +69,12 @@ def _ddp_worker(rank, world, port, out):
         gathered = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(gathered, flat)
         out[rank] = float(max((g - flat).abs().max() for g in gathered))
+        # the trainer's DDP settings (gradient bucket views, 100 MB buckets) and
+        # their override
+        tr2 = Trainer(tiny(), torch.device("cpu"), lr=1e-3, seed=0, ddp=True,
+                      ddp_kwargs={"bucket_cap_mb": 1})
+        out[f"ddp{rank}"] = (tr.model.gradient_as_bucket_view, tr.model.bucket_bytes_cap,
+                             tr2.model.bucket_bytes_cap)
     finally:
         dist.destroy_process_group()
 
@@ -78,8 +84,9 @@ def test_two_rank_data_parallel_step_keeps_replicas_identical():
     with mp.Manager() as mgr:
         out = mgr.dict()
         mp.spawn(_ddp_worker, args=(world, _free_port(), out), nprocs=world, join=True)
-        assert sorted(out.keys()) == [0, 1]
-        assert max(out.values()) == 0.0
+        assert max(out[r] for r in range(world)) == 0.0
+        for r in range(world):
+            assert out[f"ddp{r}"] == (True, 100 * 2**20, 2**20)
 
 
 @pytest.mark.gpu
