@@ -64,6 +64,27 @@ int sqb_layernorm_bwd(const void* dy, int dy_dtype, const float* x, const float*
                       float* dbias, void* workspace, size_t ws_bytes, int64_t N, int64_t C,
                       void* stream);
 
+/* Residual add fused into the LayerNorm that reads its sum (the GPT caller's
+ * x = x + block(...) followed by the next LayerNorm):
+ *   x_out = x + h   (h: fp32 or bf16 rows by h_dtype, e.g. a bf16 autocast
+ *                    Linear's output; the sum in fp32 as torch adds them),
+ *   y     = LayerNorm(x_out) as sqb_layernorm_fwd, mean and rstd of x_out.
+ * x_out and h 16-byte aligned like the other rows. */
+int sqb_add_layernorm_fwd(const float* x, const void* h, int h_dtype, float* x_out,
+                          const float* weight, const float* bias, void* y, int y_dtype,
+                          float* mean, float* rstd, int64_t N, int64_t C, float eps,
+                          void* stream);
+
+/* Its backward: dx = (LayerNorm's input gradient from dy) + dres, where dres
+ * (fp32, N x C, may be NULL) is the gradient reaching x_out from its other
+ * uses; dx is the gradient of both x and h, written as fp32 and, unless dh_bf16
+ * is NULL, also as bf16 (for a bf16 h).  dweight / dbias and the workspace as
+ * sqb_layernorm_bwd (x_out is the LayerNorm's input). */
+int sqb_add_layernorm_bwd(const void* dy, int dy_dtype, const float* x_out, const float* weight,
+                          const float* mean, const float* rstd, const float* dres, float* dx,
+                          void* dh_bf16, float* dweight, float* dbias, void* workspace,
+                          size_t ws_bytes, int64_t N, int64_t C, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,6 +80,12 @@ TRAIN_SIGNATURES = {
     "sqb_layernorm_workspace_bytes": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "sqb_layernorm_bwd": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int] + [ctypes.c_void_p] * 8 +
                           [ctypes.c_size_t, _c_i64, _c_i64, ctypes.c_void_p]),
+    "sqb_add_layernorm_fwd": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int] +
+                              [ctypes.c_void_p] * 4 + [ctypes.c_int] + [ctypes.c_void_p] * 2 +
+                              [_c_i64, _c_i64, ctypes.c_float, ctypes.c_void_p]),
+    "sqb_add_layernorm_bwd": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int] +
+                              [ctypes.c_void_p] * 10 +
+                              [ctypes.c_size_t, _c_i64, _c_i64, ctypes.c_void_p]),
 }
 
 

@@ -11,6 +11,13 @@
 // its warps in shared memory and writes one partial row per CTA, and a second
 // kernel adds the partial rows column by column: dweight and dbias come out in a
 // fixed order (bit-reproducible).
+//
+// Residual variants (sqb_add_layernorm_*): the forward first forms the row
+// x_out = x + h (h fp32 or bf16, what a bf16 autocast Linear hands the residual
+// stream) and writes it, then normalises it; the backward adds the gradient
+// reaching x_out from its other uses to the LayerNorm's dx and also writes the
+// sum as bf16 (the gradient of a bf16 h).  One pass each instead of an add, a
+// LayerNorm, a gradient add and a cast.
 
 #include <cuda_bf16.h>
 #include <math.h>
@@ -53,8 +60,10 @@ __device__ __forceinline__ void store4(__nv_bfloat16* p, float4 v) {
 // Column of lane `lane`'s k-th float4: the warp reads 512 contiguous bytes per k.
 __device__ __forceinline__ int col(int lane, int k) { return (k * 32 + lane) * 4; }
 
+// h (null, or fp32 / bf16 rows by h_bf16): x_out = x + h is written and normalised.
 template <int VPL, typename OutT>
-__global__ void __launch_bounds__(kThreads) fwd_kernel(const float* x, const float* w,
+__global__ void __launch_bounds__(kThreads) fwd_kernel(const float* x, const void* h,
+                                                       bool h_bf16, float* xo, const float* w,
                                                        const float* b, OutT* y, float* mean,
                                                        float* rstd, int64_t N, float eps) {
   constexpr int C = VPL * 128;
@@ -66,7 +75,14 @@ __global__ void __launch_bounds__(kThreads) fwd_kernel(const float* x, const flo
   float s = 0.f;
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
-    v[k] = load4(xr + col(lane, k));
+    const int c0 = col(lane, k);
+    v[k] = load4(xr + c0);
+    if (h) {
+      const float4 hv = h_bf16 ? load4(static_cast<const __nv_bfloat16*>(h) + row * C + c0)
+                               : load4(static_cast<const float*>(h) + row * C + c0);
+      v[k] = make_float4(v[k].x + hv.x, v[k].y + hv.y, v[k].z + hv.z, v[k].w + hv.w);
+      store4(xo + row * C + c0, v[k]);
+    }
     s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
   }
   const float mu = warp_sum(s) * (1.f / C);
@@ -96,10 +112,9 @@ __global__ void __launch_bounds__(kThreads) fwd_kernel(const float* x, const flo
 // without a bias, C <= 512 with one), else one.
 template <int VPL, typename DyT, bool kBias>
 __global__ void __launch_bounds__(kThreads, VPL * (kBias ? 3 : 2) <= 12 ? 2 : 1)
-    bwd_kernel(const DyT* dy, const float* x,
-                                                       const float* w, const float* mean,
-                                                       const float* rstd, float* dx,
-                                                       float* part_w, float* part_b, int64_t N) {
+    bwd_kernel(const DyT* dy, const float* x, const float* w, const float* mean,
+               const float* rstd, const float* dres, float* dx, __nv_bfloat16* dh,
+               float* part_w, float* part_b, int64_t N) {
   constexpr int C = VPL * 128;
   __shared__ float red[kWarps][C];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -137,10 +152,17 @@ __global__ void __launch_bounds__(kThreads, VPL * (kBias ? 3 : 2) <= 12 ? 2 : 1)
     }
     const float m1 = warp_sum(s1) * (1.f / C), m2 = warp_sum(s2) * (1.f / C);
 #pragma unroll
-    for (int k = 0; k < VPL; ++k)
-      store4(dx + row * C + col(lane, k),
-             make_float4(rs * (g[k].x - m1 - xh[k].x * m2), rs * (g[k].y - m1 - xh[k].y * m2),
-                         rs * (g[k].z - m1 - xh[k].z * m2), rs * (g[k].w - m1 - xh[k].w * m2)));
+    for (int k = 0; k < VPL; ++k) {
+      const int c0 = col(lane, k);
+      float4 o = make_float4(rs * (g[k].x - m1 - xh[k].x * m2), rs * (g[k].y - m1 - xh[k].y * m2),
+                             rs * (g[k].z - m1 - xh[k].z * m2), rs * (g[k].w - m1 - xh[k].w * m2));
+      if (dres) {  // the gradient reaching x_out from its other uses
+        const float4 r = load4(dres + row * C + c0);
+        o = make_float4(o.x + r.x, o.y + r.y, o.z + r.z, o.w + r.w);
+      }
+      store4(dx + row * C + c0, o);
+      if (dh) store4(dh + row * C + c0, o);
+    }
   }
   // this CTA's column sums: dweight, then dbias (when asked for)
 #pragma unroll 1
@@ -193,22 +215,23 @@ int part_rows(int64_t N) {
 }
 
 template <int VPL>
-int launch_fwd(const float* x, const float* w, const float* b, void* y, int y_dtype, float* mean,
-               float* rstd, int64_t N, float eps, cudaStream_t s) {
+int launch_fwd(const float* x, const void* h, bool h_bf16, float* xo, const float* w,
+               const float* b, void* y, int y_dtype, float* mean, float* rstd, int64_t N,
+               float eps, cudaStream_t s) {
   const dim3 grid((unsigned)((N + kWarps - 1) / kWarps));
   if (y_dtype == SQB_BF16)
     fwd_kernel<VPL, __nv_bfloat16><<<grid, kThreads, 0, s>>>(
-        x, w, b, static_cast<__nv_bfloat16*>(y), mean, rstd, N, eps);
+        x, h, h_bf16, xo, w, b, static_cast<__nv_bfloat16*>(y), mean, rstd, N, eps);
   else
-    fwd_kernel<VPL, float><<<grid, kThreads, 0, s>>>(x, w, b, static_cast<float*>(y), mean,
-                                                     rstd, N, eps);
+    fwd_kernel<VPL, float><<<grid, kThreads, 0, s>>>(x, h, h_bf16, xo, w, b,
+                                                     static_cast<float*>(y), mean, rstd, N, eps);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
 }
 
 template <int VPL>
 int launch_bwd(const void* dy, int dy_dtype, const float* x, const float* w, const float* mean,
-               const float* rstd, float* dx, float* dw, float* db, float* part, int64_t N,
-               cudaStream_t s) {
+               const float* rstd, const float* dres, float* dx, __nv_bfloat16* dh, float* dw,
+               float* db, float* part, int64_t N, cudaStream_t s) {
   constexpr int C = VPL * 128;
   const int rows = part_rows(N);
   float* part_w = part;
@@ -216,17 +239,17 @@ int launch_bwd(const void* dy, int dy_dtype, const float* x, const float* w, con
   auto dyb = static_cast<const __nv_bfloat16*>(dy);
   auto dyf = static_cast<const float*>(dy);
   if (dy_dtype == SQB_BF16 && db)
-    bwd_kernel<VPL, __nv_bfloat16, true><<<rows, kThreads, 0, s>>>(dyb, x, w, mean, rstd, dx,
-                                                                    part_w, part_b, N);
+    bwd_kernel<VPL, __nv_bfloat16, true><<<rows, kThreads, 0, s>>>(
+        dyb, x, w, mean, rstd, dres, dx, dh, part_w, part_b, N);
   else if (dy_dtype == SQB_BF16)
-    bwd_kernel<VPL, __nv_bfloat16, false><<<rows, kThreads, 0, s>>>(dyb, x, w, mean, rstd, dx,
-                                                                     part_w, part_b, N);
+    bwd_kernel<VPL, __nv_bfloat16, false><<<rows, kThreads, 0, s>>>(
+        dyb, x, w, mean, rstd, dres, dx, dh, part_w, part_b, N);
   else if (db)
-    bwd_kernel<VPL, float, true><<<rows, kThreads, 0, s>>>(dyf, x, w, mean, rstd, dx, part_w,
-                                                            part_b, N);
+    bwd_kernel<VPL, float, true><<<rows, kThreads, 0, s>>>(dyf, x, w, mean, rstd, dres, dx, dh,
+                                                            part_w, part_b, N);
   else
-    bwd_kernel<VPL, float, false><<<rows, kThreads, 0, s>>>(dyf, x, w, mean, rstd, dx, part_w,
-                                                             part_b, N);
+    bwd_kernel<VPL, float, false><<<rows, kThreads, 0, s>>>(dyf, x, w, mean, rstd, dres, dx,
+                                                             dh, part_w, part_b, N);
   colsum_kernel<<<(C + 31) / 32, 256, 0, s>>>(part_w, dw, rows, C);
   if (db) colsum_kernel<<<(C + 31) / 32, 256, 0, s>>>(part_b, db, rows, C);
   return cudaGetLastError() == cudaSuccess ? SQB_OK : SQB_ERR_LAUNCH;
@@ -243,49 +266,96 @@ extern "C" size_t sqb_layernorm_workspace_bytes(int64_t N, int64_t C) {
   return (size_t)part_rows(N) * (size_t)C * 2 * sizeof(float);
 }
 
+namespace {
+
+int fwd_dispatch(const float* x, const void* h, int h_dtype, float* x_out, const float* weight,
+                 const float* bias, void* y, int y_dtype, float* mean, float* rstd, int64_t N,
+                 int64_t C, float eps, void* stream) {
+  if (!x || !weight || !y || !mean || !rstd || N <= 0 || N > ((int64_t)1 << 31) * kWarps)
+    return SQB_ERR_ARG;
+  if (h && !x_out) return SQB_ERR_ARG;
+  if (y_dtype != SQB_F32 && y_dtype != SQB_BF16) return SQB_ERR_DTYPE;
+  if (h && h_dtype != SQB_F32 && h_dtype != SQB_BF16) return SQB_ERR_DTYPE;
+  if (C <= 0 || C % 128 != 0 || C / 128 > kMaxVpl) return SQB_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(weight) || (bias && !aligned16(bias)) || !aligned16(y) ||
+      (h && (!aligned16(h) || !aligned16(x_out))))
+    return SQB_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool hb = h_dtype == SQB_BF16;
+#define SQB_LN_FWD(V) launch_fwd<V>(x, h, hb, x_out, weight, bias, y, y_dtype, mean, rstd, N, eps, s)
+  switch (C / 128) {
+    case 1: return SQB_LN_FWD(1);
+    case 2: return SQB_LN_FWD(2);
+    case 3: return SQB_LN_FWD(3);
+    case 4: return SQB_LN_FWD(4);
+    case 5: return SQB_LN_FWD(5);
+    case 6: return SQB_LN_FWD(6);
+    case 7: return SQB_LN_FWD(7);
+    default: return SQB_LN_FWD(8);
+  }
+#undef SQB_LN_FWD
+}
+
+int bwd_dispatch(const void* dy, int dy_dtype, const float* x, const float* weight,
+                 const float* mean, const float* rstd, const float* dres, float* dx, void* dh,
+                 float* dweight, float* dbias, void* workspace, size_t ws_bytes, int64_t N,
+                 int64_t C, void* stream) {
+  if (!dy || !x || !weight || !mean || !rstd || !dx || !dweight || N <= 0) return SQB_ERR_ARG;
+  if (dy_dtype != SQB_F32 && dy_dtype != SQB_BF16) return SQB_ERR_DTYPE;
+  if (C <= 0 || C % 128 != 0 || C / 128 > kMaxVpl) return SQB_ERR_UNSUPPORTED;
+  if (!workspace || ws_bytes < sqb_layernorm_workspace_bytes(N, C)) return SQB_ERR_WORKSPACE;
+  if (!aligned16(dy) || !aligned16(x) || !aligned16(weight) || !aligned16(dx) ||
+      !aligned16(workspace) || (dres && !aligned16(dres)) || (dh && !aligned16(dh)))
+    return SQB_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  auto* dhb = static_cast<__nv_bfloat16*>(dh);
+#define SQB_LN_BWD(V) \
+  launch_bwd<V>(dy, dy_dtype, x, weight, mean, rstd, dres, dx, dhb, dweight, dbias, part, N, s)
+  switch (C / 128) {
+    case 1: return SQB_LN_BWD(1);
+    case 2: return SQB_LN_BWD(2);
+    case 3: return SQB_LN_BWD(3);
+    case 4: return SQB_LN_BWD(4);
+    case 5: return SQB_LN_BWD(5);
+    case 6: return SQB_LN_BWD(6);
+    case 7: return SQB_LN_BWD(7);
+    default: return SQB_LN_BWD(8);
+  }
+#undef SQB_LN_BWD
+}
+
+}  // namespace
+
 extern "C" int sqb_layernorm_fwd(const float* x, const float* weight, const float* bias, void* y,
                                  int y_dtype, float* mean, float* rstd, int64_t N, int64_t C,
                                  float eps, void* stream) {
-  if (!x || !weight || !y || !mean || !rstd || N <= 0 || N > ((int64_t)1 << 31) * kWarps)
-    return SQB_ERR_ARG;
-  if (y_dtype != SQB_F32 && y_dtype != SQB_BF16) return SQB_ERR_DTYPE;
-  if (C <= 0 || C % 128 != 0 || C / 128 > kMaxVpl) return SQB_ERR_UNSUPPORTED;
-  if (!aligned16(x) || !aligned16(weight) || (bias && !aligned16(bias)) || !aligned16(y))
-    return SQB_ERR_ALIGN;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (C / 128) {
-    case 1: return launch_fwd<1>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-    case 2: return launch_fwd<2>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-    case 3: return launch_fwd<3>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-    case 4: return launch_fwd<4>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-    case 5: return launch_fwd<5>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-    case 6: return launch_fwd<6>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-    case 7: return launch_fwd<7>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-    default: return launch_fwd<8>(x, weight, bias, y, y_dtype, mean, rstd, N, eps, s);
-  }
+  return fwd_dispatch(x, nullptr, SQB_F32, nullptr, weight, bias, y, y_dtype, mean, rstd, N, C,
+                      eps, stream);
 }
 
 extern "C" int sqb_layernorm_bwd(const void* dy, int dy_dtype, const float* x,
                                  const float* weight, const float* mean, const float* rstd,
                                  float* dx, float* dweight, float* dbias, void* workspace,
                                  size_t ws_bytes, int64_t N, int64_t C, void* stream) {
-  if (!dy || !x || !weight || !mean || !rstd || !dx || !dweight || N <= 0) return SQB_ERR_ARG;
-  if (dy_dtype != SQB_F32 && dy_dtype != SQB_BF16) return SQB_ERR_DTYPE;
-  if (C <= 0 || C % 128 != 0 || C / 128 > kMaxVpl) return SQB_ERR_UNSUPPORTED;
-  if (!workspace || ws_bytes < sqb_layernorm_workspace_bytes(N, C)) return SQB_ERR_WORKSPACE;
-  if (!aligned16(dy) || !aligned16(x) || !aligned16(weight) || !aligned16(dx) ||
-      !aligned16(workspace))
-    return SQB_ERR_ALIGN;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  float* part = static_cast<float*>(workspace);
-  switch (C / 128) {
-    case 1: return launch_bwd<1>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-    case 2: return launch_bwd<2>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-    case 3: return launch_bwd<3>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-    case 4: return launch_bwd<4>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-    case 5: return launch_bwd<5>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-    case 6: return launch_bwd<6>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-    case 7: return launch_bwd<7>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-    default: return launch_bwd<8>(dy, dy_dtype, x, weight, mean, rstd, dx, dweight, dbias, part, N, s);
-  }
+  return bwd_dispatch(dy, dy_dtype, x, weight, mean, rstd, nullptr, dx, nullptr, dweight, dbias,
+                      workspace, ws_bytes, N, C, stream);
+}
+
+extern "C" int sqb_add_layernorm_fwd(const float* x, const void* h, int h_dtype, float* x_out,
+                                     const float* weight, const float* bias, void* y,
+                                     int y_dtype, float* mean, float* rstd, int64_t N,
+                                     int64_t C, float eps, void* stream) {
+  if (!h) return SQB_ERR_ARG;
+  return fwd_dispatch(x, h, h_dtype, x_out, weight, bias, y, y_dtype, mean, rstd, N, C, eps,
+                      stream);
+}
+
+extern "C" int sqb_add_layernorm_bwd(const void* dy, int dy_dtype, const float* x_out,
+                                     const float* weight, const float* mean, const float* rstd,
+                                     const float* dres, float* dx, void* dh_bf16,
+                                     float* dweight, float* dbias, void* workspace,
+                                     size_t ws_bytes, int64_t N, int64_t C, void* stream) {
+  return bwd_dispatch(dy, dy_dtype, x_out, weight, mean, rstd, dres, dx, dh_bf16, dweight,
+                      dbias, workspace, ws_bytes, N, C, stream);
 }

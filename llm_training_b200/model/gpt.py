@@ -17,7 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from ..ops import layer_norm, layer_norm_supported
+from ..ops import add_layer_norm, add_layer_norm_supported, layer_norm, layer_norm_supported
 from .attention_registry import build_attention
 
 
@@ -28,17 +28,33 @@ class LayerNorm(nn.Module):
         if not bias:
             self.ln.register_parameter("bias", None)
 
+    @staticmethod
+    def _out_dtype():
+        out = torch.float32
+        if torch.is_autocast_enabled("cuda"):
+            out = torch.get_autocast_dtype("cuda")
+        return out if out in (torch.float32, torch.bfloat16) else None
+
     def forward(self, x):
         # CUDA fp32 rows (the residual stream): the library's fused LayerNorm,
         # fp32 math as nn.LayerNorm under autocast, its output written directly
         # in the autocast dtype that every consumer here (a Linear) casts it to
         if layer_norm_supported(x, self.ln.weight):
-            out = torch.float32
-            if torch.is_autocast_enabled("cuda"):
-                out = torch.get_autocast_dtype("cuda")
-            if out in (torch.float32, torch.bfloat16):
+            out = self._out_dtype()
+            if out is not None:
                 return layer_norm(x, self.ln.weight, self.ln.bias, self.ln.eps, out)
         return self.ln(x)
+
+    def add_forward(self, x, h):
+        """(x + h, this LayerNorm of x + h): the residual add and the LayerNorm
+        that reads its sum, as one kernel each way on the CUDA fp32 residual
+        stream (the same fp32 sum and LayerNorm as the two separate ops)."""
+        if add_layer_norm_supported(x, h, self.ln.weight):
+            out = self._out_dtype()
+            if out is not None:
+                return add_layer_norm(x, h, self.ln.weight, self.ln.bias, self.ln.eps, out)
+        x = x + h
+        return x, self(x)
 
 
 class MLP(nn.Module):
@@ -124,9 +140,15 @@ class GPT(nn.Module):
             f"Cannot forward sequence of length {t}, block size is only {self.config.block_size}")
         pos = torch.arange(0, t, dtype=torch.long, device=idx.device)
         x = self.transformer.drop(self.transformer.wte(idx) + self.transformer.wpe(pos))
-        for block in self.transformer.attn_blocks:
-            x = block(x)
-        h = self.transformer.ln_(x)
+        # the blocks' residual stream (Attention_Block.forward, unrolled): each
+        # residual add goes into the LayerNorm that next reads the stream - the
+        # block's second one, the next block's first, or the final one
+        blocks = self.transformer.attn_blocks
+        h = (blocks[0].lm1 if len(blocks) else self.transformer.ln_)(x)
+        for i, block in enumerate(blocks):
+            x, y = block.lm2.add_forward(x, block.attn(h))
+            nxt = blocks[i + 1].lm1 if i + 1 < len(blocks) else self.transformer.ln_
+            x, h = nxt.add_forward(x, block.mlp(y))
         V = self.config.vocab_size
         if not pad_vocab or V % self.VOCAB_ALIGN == 0:
             return self.lm_head(h)

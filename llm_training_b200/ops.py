@@ -614,6 +614,110 @@ def _layernorm_grad(ctx, dy, _dmean, _drstd):
 _layernorm_fwd.register_autograd(_layernorm_grad, setup_context=_layernorm_setup)
 
 
+@torch.library.custom_op("sqrtblock::add_layernorm_fwd", mutates_args=())
+def _add_layernorm_fwd(x2: torch.Tensor, h2: torch.Tensor, w: torch.Tensor,
+                       b: Optional[torch.Tensor], eps: float, out_dtype: torch.dtype
+                       ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Rows x2 (N, C) fp32 and h2 (N, C) fp32/bf16 -> (x2 + h2 fp32, its LayerNorm in
+    out_dtype, mean, rstd)."""
+    N, C = x2.shape
+    xo = torch.empty((N, C), dtype=torch.float32, device=x2.device)
+    y = torch.empty((N, C), dtype=out_dtype, device=x2.device)
+    mean = torch.empty(N, dtype=torch.float32, device=x2.device)
+    rstd = torch.empty(N, dtype=torch.float32, device=x2.device)
+    stream = torch.cuda.current_stream(x2.device).cuda_stream
+    _lib.check("sqb_add_layernorm_fwd", _lib.lib().sqb_add_layernorm_fwd(
+        x2.data_ptr(), h2.data_ptr(), _DTYPES[h2.dtype], xo.data_ptr(), w.data_ptr(),
+        b.data_ptr() if b is not None else None, y.data_ptr(), _DTYPES[out_dtype],
+        mean.data_ptr(), rstd.data_ptr(), N, C, float(eps), stream))
+    return xo, y, mean, rstd
+
+
+@_add_layernorm_fwd.register_fake
+def _(x2, h2, w, b, eps, out_dtype):
+    N, C = x2.shape
+    f32 = torch.float32
+    return (x2.new_empty((N, C), dtype=f32), x2.new_empty((N, C), dtype=out_dtype),
+            x2.new_empty((N,), dtype=f32), x2.new_empty((N,), dtype=f32))
+
+
+@torch.library.custom_op("sqrtblock::add_layernorm_bwd", mutates_args=())
+def _add_layernorm_bwd(dy2: torch.Tensor, xo2: torch.Tensor, w: torch.Tensor,
+                       mean: torch.Tensor, rstd: torch.Tensor, dres: Optional[torch.Tensor],
+                       has_bias: bool, h_bf16: bool
+                       ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dx fp32 = the gradient of x and h, dh as bf16 (empty unless h_bf16), dw, db)."""
+    N, C = xo2.shape
+    dx = torch.empty((N, C), dtype=torch.float32, device=xo2.device)
+    dh = torch.empty((N, C) if h_bf16 else (0,), dtype=torch.bfloat16, device=xo2.device)
+    dw = torch.empty(C, dtype=torch.float32, device=xo2.device)
+    db = torch.empty(C if has_bias else 0, dtype=torch.float32, device=xo2.device)
+    wsb = _lib.lib().sqb_layernorm_workspace_bytes(N, C)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=xo2.device)
+    stream = torch.cuda.current_stream(xo2.device).cuda_stream
+    _lib.check("sqb_add_layernorm_bwd", _lib.lib().sqb_add_layernorm_bwd(
+        dy2.data_ptr(), _DTYPES[dy2.dtype], xo2.data_ptr(), w.data_ptr(), mean.data_ptr(),
+        rstd.data_ptr(), dres.data_ptr() if dres is not None else None, dx.data_ptr(),
+        dh.data_ptr() if h_bf16 else None, dw.data_ptr(),
+        db.data_ptr() if has_bias else None, ws.data_ptr(), wsb, N, C, stream))
+    return dx, dh, dw, db
+
+
+@_add_layernorm_bwd.register_fake
+def _(dy2, xo2, w, mean, rstd, dres, has_bias, h_bf16):
+    N, C = xo2.shape
+    f32 = torch.float32
+    return (xo2.new_empty((N, C), dtype=f32),
+            xo2.new_empty((N, C) if h_bf16 else (0,), dtype=torch.bfloat16),
+            xo2.new_empty((C,), dtype=f32), xo2.new_empty((C if has_bias else 0,), dtype=f32))
+
+
+def _add_layernorm_setup(ctx, inputs, output):
+    x2, h2, w, b, eps, out_dtype = inputs
+    xo, _, mean, rstd = output
+    ctx.save_for_backward(xo, w, mean, rstd)
+    ctx.has_bias = b is not None
+    ctx.h_dtype = h2.dtype
+    ctx.mark_non_differentiable(mean, rstd)
+
+
+def _add_layernorm_grad(ctx, dxo, dy, _dmean, _drstd):
+    xo, w, mean, rstd = ctx.saved_tensors
+    N, C = xo.shape
+    if dy is None:
+        dy = torch.zeros((N, C), dtype=torch.float32, device=xo.device)
+    dy2 = dy.reshape(N, C)
+    if dy2.dtype not in _DTYPES:
+        dy2 = dy2.float()
+    dres = dxo.reshape(N, C).float().contiguous() if dxo is not None else None
+    h_bf16 = ctx.h_dtype == torch.bfloat16
+    dx, dh, dw, db = _add_layernorm_bwd(dy2.contiguous(), xo, w, mean, rstd, dres,
+                                        ctx.has_bias, h_bf16)
+    dh_out = dh if h_bf16 else dx.to(ctx.h_dtype, copy=True)
+    return dx, dh_out, dw, (db if ctx.has_bias else None), None, None
+
+
+_add_layernorm_fwd.register_autograd(_add_layernorm_grad, setup_context=_add_layernorm_setup)
+
+
+def add_layer_norm(x, h, weight, bias=None, eps=1e-5, out_dtype=torch.float32):
+    """(x + h, LayerNorm(x + h)) for CUDA fp32 ``x`` and fp32 or bf16 ``h`` of the same
+    shape (``layer_norm_supported(x, weight)``): the sum in fp32 as torch adds them,
+    the LayerNorm as ``layer_norm``; one kernel each way (the
+    ``sqrtblock::add_layernorm_fwd/bwd`` custom ops)."""
+    C = x.shape[-1]
+    x2 = x.reshape(-1, C).contiguous()
+    h2 = h.reshape(-1, C).contiguous()
+    b = bias.contiguous() if bias is not None else None
+    xo, y, _, _ = _add_layernorm_fwd(x2, h2, weight.contiguous(), b, float(eps), out_dtype)
+    return xo.view(x.shape), y.view(x.shape)
+
+
+def add_layer_norm_supported(x, h, weight) -> bool:
+    return (layer_norm_supported(x, weight) and h.shape == x.shape and h.is_cuda
+            and h.dtype in (torch.float32, torch.bfloat16))
+
+
 def layer_norm(x, weight, bias=None, eps=1e-5, out_dtype=torch.float32):
     """LayerNorm over the last dimension of CUDA fp32 ``x`` (see
     ``layer_norm_supported``), fp32 math; the output in ``out_dtype`` (fp32, or

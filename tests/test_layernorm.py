@@ -79,3 +79,65 @@ def test_gpt_layernorm_module_matches_nn_layernorm_under_autocast():
     (gx,) = torch.autograd.grad(y.float().sum(), x)
     (gx_ref,) = torch.autograd.grad(y_ref.to(torch.bfloat16).float().sum(), x)
     torch.testing.assert_close(gx, gx_ref, rtol=1e-4, atol=1e-4)
+
+
+def test_add_variant_rejects_bad_arguments_without_a_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(256)
+    # no h, or h without an x_out destination
+    assert lib.sqb_add_layernorm_fwd(p, None, 0, p, p, None, p, 0, p, p, 4, 128, 1e-5,
+                                     None) == ERR_ARG
+    assert lib.sqb_add_layernorm_fwd(p, p, 0, None, p, None, p, 0, p, p, 4, 128, 1e-5,
+                                     None) == ERR_ARG
+    assert lib.sqb_add_layernorm_bwd(p, 0, p, p, p, p, None, p, None, p, None, p, 16, 4, 128,
+                                     None) == ERR_WORKSPACE
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,C,bias,ht,out,with_res", [
+    (1000, 768, False, torch.bfloat16, torch.bfloat16, True),
+    (4097, 1024, True, torch.bfloat16, torch.bfloat16, False),
+    (3, 128, True, torch.float32, torch.float32, True),
+    (5003, 384, False, torch.float32, torch.bfloat16, True),
+])
+def test_add_layer_norm_matches_add_then_layer_norm(N, C, bias, ht, out, with_res):
+    """(x + h, LayerNorm(x + h)) and its gradients against torch's add and
+    F.layer_norm in fp32; the residual output's own downstream gradient (with_res)
+    joins the LayerNorm's input gradient."""
+    from llm_training_b200.ops import add_layer_norm
+
+    g = torch.Generator().manual_seed(N + 7 * C)
+    x = (torch.randn(N, C, generator=g) * 2 + 0.5).cuda()
+    h = torch.randn(N, C, generator=g).to(ht).cuda()
+    w = (1 + 0.1 * torch.randn(C, generator=g)).cuda()
+    b = (0.1 * torch.randn(C, generator=g)).cuda() if bias else None
+    dy = torch.randn(N, C, generator=g).to(out).cuda()
+    dxo = torch.randn(N, C, generator=g).cuda()
+
+    def leaves():
+        return (x.clone().requires_grad_(True), h.clone().requires_grad_(True),
+                w.clone().requires_grad_(True), b.clone().requires_grad_(True) if bias else None)
+
+    xs, hs, ws, bs = leaves()
+    xo, y = add_layer_norm(xs, hs, ws, bs, 1e-5, out)
+    assert xo.dtype == torch.float32 and y.dtype == out
+    outs, grads = ((xo, y), (dxo, dy)) if with_res else ((y,), (dy,))
+    torch.autograd.backward(outs, grads)
+    xr, hr, wr, br = leaves()
+    xor = xr + hr
+    yr = F.layer_norm(xor, (C,), wr, br, 1e-5)
+    outs_r, grads_r = ((xor, yr), (dxo, dy.float())) if with_res else ((yr,), (dy.float(),))
+    torch.autograd.backward(outs_r, grads_r)
+    torch.testing.assert_close(xo, xor, rtol=0, atol=0)  # the same fp32 sum
+    if out == torch.float32:
+        torch.testing.assert_close(y, yr, rtol=1e-5, atol=1e-5)
+    else:
+        torch.testing.assert_close(y.float(), yr, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(xs.grad, xr.grad, rtol=1e-4, atol=1e-4)
+    assert hs.grad.dtype == ht
+    torch.testing.assert_close(hs.grad.float(), hr.grad.float(),
+                               rtol=1e-2 if ht == torch.bfloat16 else 1e-4,
+                               atol=1e-2 if ht == torch.bfloat16 else 1e-4)
+    torch.testing.assert_close(ws.grad, wr.grad, rtol=1e-4, atol=1e-3)
+    if bias:
+        torch.testing.assert_close(bs.grad, br.grad, rtol=1e-4, atol=1e-3)

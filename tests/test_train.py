@@ -132,9 +132,10 @@ def test_padded_vocab_logits_give_the_same_loss_and_gradients():
 
 @pytest.mark.gpu
 def test_gpu_fused_caller_ops_match_torch_ops_end_to_end(monkeypatch):
-    """One autocast step of a small GPT: the fused LayerNorm, the fused
-    cross-entropy and the padded-vocabulary logits give the loss and gradients
-    of the same model on nn.LayerNorm, F.cross_entropy and unpadded logits."""
+    """One autocast step of a small GPT: the fused LayerNorm (and residual add +
+    LayerNorm), the fused cross-entropy and the padded-vocabulary logits give the
+    loss and gradients of the same model on torch's add, nn.LayerNorm,
+    F.cross_entropy and unpadded logits."""
     import torch.nn.functional as F
 
     import llm_training_b200.model.gpt as gpt_mod
@@ -162,6 +163,7 @@ def test_gpu_fused_caller_ops_match_torch_ops_end_to_end(monkeypatch):
     l_fused, g_fused = run(True)
     with monkeypatch.context() as mp_:
         mp_.setattr(gpt_mod, "layer_norm_supported", lambda *a: False)
+        mp_.setattr(gpt_mod, "add_layer_norm_supported", lambda *a: False)
         l_ref, g_ref = run(False)
     # the same values reach every bf16 GEMM; the LayerNorm statistics are summed
     # in a different order, which bf16 rounding can amplify by an ulp here and there
