@@ -194,8 +194,10 @@ def sqrt_block_forward(q, k, v, block=None, scale=None, impl="auto"):
 
 
 def sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block=None, scale=None,
-                        impl="auto"):
-    """Backward from saved forward outputs -> (dq, dk, dv), each (B, T, H, D)."""
+                        impl="auto", out=None):
+    """Backward from saved forward outputs -> (dq, dk, dv), each (B, T, H, D).
+    ``out``: three (B, T, H, D) views (unit stride on D) to write them into, e.g.
+    the thirds of one packed (B, T, 3C) gradient."""
     q, k, v, o = _prep(q, "q"), _prep(k, "k"), _prep(v, "v"), _prep(o, "o")
     dout = _prep(dout, "dout")
     if dout.dtype != q.dtype:
@@ -207,9 +209,17 @@ def sqrt_block_backward(q, k, v, o, lse, kbar, vbar, dout, block=None, scale=Non
     dev = q.device
     if _mailbox_words:
         check_status(dev)
-    dq = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
-    dk = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
-    dv = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+    if out is not None:
+        dq, dk, dv = out
+        for t in out:
+            if (t.shape != (B, T, H, D) or t.dtype != q.dtype or t.device != dev
+                    or t.stride(-1) != 1):
+                raise ValueError("out must be three (B, T, H, D) tensors of q's dtype and "
+                                 "device with unit stride on D")
+    else:
+        dq = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+        dk = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
+        dv = torch.empty((B, T, H, D), dtype=q.dtype, device=dev)
     ws = _workspace(dev, (B, T, H, D, b))
     stream = torch.cuda.current_stream(dev).cuda_stream
     st = _lib.strides_array(*(_strides(t) for t in (q, k, v, o, dout, dq, dk, dv)))
@@ -305,6 +315,72 @@ def _attention_grad(ctx, dout, _dlse, _dkbar, _dvbar):
 
 
 _attention_fwd.register_autograd(_attention_grad, setup_context=_attention_setup)
+
+
+def _split_qkv(qkv, n_head):
+    """The thirds of a packed (B, T, 3C) projection as (B, T, H, D) views."""
+    B, T, C3 = qkv.shape
+    C = C3 // 3
+    return tuple(qkv[..., i * C:(i + 1) * C].view(B, T, n_head, C // n_head) for i in range(3))
+
+
+@torch.library.custom_op("sqrtblock::attention_qkv_fwd", mutates_args=())
+def _attention_qkv_fwd(qkv: torch.Tensor, n_head: int, block: Optional[int],
+                       scale: Optional[float], impl: str
+                       ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    return sqrt_block_forward(*_split_qkv(qkv, n_head), block, scale, impl)
+
+
+@_attention_qkv_fwd.register_fake
+def _(qkv, n_head, block, scale, impl):
+    B, T, C3 = qkv.shape
+    H, D = n_head, C3 // 3 // n_head
+    _, _, Gc = _fake_geometry(T, block)
+    return (qkv.new_empty((B, T, H, D)), qkv.new_empty((B, H, T), dtype=torch.float32),
+            qkv.new_empty((B, H, Gc, D)), qkv.new_empty((B, H, Gc, D)))
+
+
+@torch.library.custom_op("sqrtblock::attention_qkv_bwd", mutates_args=())
+def _attention_qkv_bwd(qkv: torch.Tensor, o: torch.Tensor, lse: torch.Tensor,
+                       kbar: torch.Tensor, vbar: torch.Tensor, dout: torch.Tensor, n_head: int,
+                       block: Optional[int], scale: Optional[float], impl: str) -> torch.Tensor:
+    """dQ, dK, dV written straight into the thirds of one packed (B, T, 3C) gradient."""
+    dqkv = torch.empty(qkv.shape, dtype=qkv.dtype, device=qkv.device)
+    sqrt_block_backward(*_split_qkv(qkv, n_head), o, lse, kbar, vbar, dout, block, scale, impl,
+                        out=_split_qkv(dqkv, n_head))
+    return dqkv
+
+
+@_attention_qkv_bwd.register_fake
+def _(qkv, o, lse, kbar, vbar, dout, n_head, block, scale, impl):
+    return qkv.new_empty(qkv.shape)
+
+
+def _attention_qkv_setup(ctx, inputs, output):
+    qkv, n_head, block, scale, impl = inputs
+    o, lse, kbar, vbar = output
+    ctx.save_for_backward(qkv, o, lse, kbar, vbar)
+    ctx.cfg = (n_head, block, scale, impl)
+    ctx.mark_non_differentiable(lse, kbar, vbar)
+
+
+def _attention_qkv_grad(ctx, dout, _dlse, _dkbar, _dvbar):
+    qkv, o, lse, kbar, vbar = ctx.saved_tensors
+    return _attention_qkv_bwd(qkv, o, lse, kbar, vbar, dout, *ctx.cfg), None, None, None, None
+
+
+_attention_qkv_fwd.register_autograd(_attention_qkv_grad, setup_context=_attention_qkv_setup)
+
+
+def sqrt_block_attention_qkv(qkv, n_head, block=None, scale=None, impl="auto"):
+    """``sqrt_block_attention`` on the thirds (Q, K, V) of one packed (B, T, 3C)
+    projection, contiguous, C = n_head * D: the kernels read it in place, and the
+    backward writes dQ, dK, dV into one (B, T, 3C) gradient, so the projection's
+    backward is a single GEMM and needs no gradient adds (the
+    ``sqrtblock::attention_qkv_fwd/bwd`` custom ops)."""
+    if qkv.dim() != 3 or qkv.shape[-1] % (3 * n_head) != 0:
+        raise ValueError(f"qkv must be (B, T, 3 * n_head * D), got {tuple(qkv.shape)}")
+    return _attention_qkv_fwd(qkv.contiguous(), int(n_head), block, scale, impl)[0]
 
 
 def sqrt_block_attention(q, k, v, block=None, scale=None, impl="auto"):
