@@ -150,24 +150,28 @@ __global__ void delta_kernel(Problem p, TensorView o, TensorView dout, float* de
   if (lane == 0) delta[(int64_t)bh * p.T + t] = s;
 }
 
-// Summary gradients: one warp per (summary j, bh) walks every later query.
+// Summary gradients: one CTA per (summary j, bh); its warps split the later
+// queries (warp w takes t = first + w, first + w + 8, ...) and add their
+// partial sums in shared memory in warp order, so the result does not depend on
+// scheduling (one warp walking every later query made the first summaries'
+// chains the kernel's length).
 //   dKbar_j = scale * sum_t ds_tj q_t,  dVbar_j = sum_t p_tj dO_t.
 template <typename E>
-__global__ void summary_grad_kernel(Problem p, TensorView q, TensorView dout, const float* lse,
-                                    const float* delta, const E* kbar, const E* vbar,
-                                    float* dkbar, float* dvbar) {
-  const int lane = threadIdx.x & 31;
-  const int j = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) summary_grad_kernel(
+    Problem p, TensorView q, TensorView dout, const float* lse, const float* delta,
+    const E* kbar, const E* vbar, float* dkbar, float* dvbar) {
+  __shared__ float red[2][kWarpsPerBlock][32 * kMaxPerLane];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = blockIdx.x;
   const int bh = blockIdx.y;
   const int n = bh / p.H, h = bh % p.H;
-  if (j >= p.Gc) return;
   const int64_t soff = ((int64_t)bh * p.Gc + j) * p.D;
   float kb[kMaxPerLane], vb[kMaxPerLane], gk[kMaxPerLane], gv[kMaxPerLane];
   load_row(kbar + soff, p.D, lane, kb);
   load_row(vbar + soff, p.D, lane, vb);
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) gk[i] = gv[i] = 0.f;
-  for (int t = (j + 1) * p.b; t < p.T; ++t) {
+  for (int t = (j + 1) * p.b + warp; t < p.T; t += kWarpsPerBlock) {
     const E* qr = row_ptr<E>(q, n, t, h);
     const E* dr = row_ptr<E>(dout, n, t, h);
     const float s = dot_row(qr, p.D, lane, kb) * p.scale;
@@ -185,11 +189,19 @@ __global__ void summary_grad_kernel(Problem p, TensorView q, TensorView dout, co
   }
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
-    int d = lane + 32 * i;
-    if (d < p.D) {
-      dkbar[soff + d] = gk[i] * p.scale;
-      dvbar[soff + d] = gv[i];
+    red[0][warp][lane + 32 * i] = gk[i];
+    red[1][warp][lane + 32 * i] = gv[i];
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < p.D; d += 32 * kWarpsPerBlock) {
+    float sk = 0.f, sv = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarpsPerBlock; ++w) {
+      sk += red[0][w][d];
+      sv += red[1][w][d];
     }
+    dkbar[soff + d] = sk * p.scale;
+    dvbar[soff + d] = sv;
   }
 }
 
@@ -321,7 +333,7 @@ int backward_t(const Problem& p, TensorView q, TensorView k, TensorView v, Tenso
   delta_kernel<E><<<rows, nt, 0, s>>>(p, o, dout, delta);
   if (int e = launch_status()) return e;
   if (p.Gc > 0) {
-    dim3 sg((p.Gc + kWarpsPerBlock - 1) / kWarpsPerBlock, BH);
+    dim3 sg(p.Gc, BH);
     summary_grad_kernel<E><<<sg, nt, 0, s>>>(p, q, dout, lse, delta, (const E*)kbar,
                                              (const E*)vbar, dkbar, dvbar);
     if (int e = launch_status()) return e;
